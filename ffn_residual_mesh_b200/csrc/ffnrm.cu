@@ -1,0 +1,645 @@
+// C ABI of the B200 exact base/residual split (see include/ffnrm.h).
+//
+// One context per device: owns each layer's device weights (codes in the layouts of
+// ffnrm_common.cuh, alpha/beta, fp16 down), a workspace sized for max_tokens, and a
+// non-blocking copy stream plus events for the host-streamed base pipeline.
+#include "ffnrm.h"
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "down_gemv.cuh"
+#include "ffnrm_common.cuh"
+#include "residual_dp4a.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+#define FFNRM_CUDA(expr)                                                                          \
+    do {                                                                                          \
+        cudaError_t _e = (expr);                                                                  \
+        if (_e != cudaSuccess)                                                                    \
+            return fail(FFNRM_ERR_CUDA, "%s failed at %s:%d: %s", #expr, __FILE__, __LINE__,      \
+                        cudaGetErrorString(_e));                                                  \
+    } while (0)
+
+struct DevBuf {
+    void *ptr = nullptr;
+    size_t bytes = 0;
+};
+
+struct LayerDev {
+    bool loaded = false;
+    bool scales_half = true;
+    bool has_fallback = false;
+    DevBuf pair[2], plane[2], pair_hi[2], alpha[2], beta[2], down;
+};
+
+}  // namespace
+
+struct ffnrm_ctx {
+    int device = 0;
+    ffnrm_config cfg{};
+    int G = 0;
+    std::vector<LayerDev> layers;
+    // workspace
+    float *res[2] = {nullptr, nullptr};  // [Tm, F]
+    float *partial = nullptr;            // [max_splits, Tm, D]
+    int max_splits = 16;
+    // host-streamed mode staging
+    int8_t *z_dev = nullptr;
+    float *s_dev = nullptr;
+    float *base_dev[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};  // [slot][proj] [Tm, F]
+    uint8_t *tiles_dev[2] = {nullptr, nullptr};
+    uint16_t *y16_dev = nullptr;
+    cudaStream_t copy_stream = nullptr;
+    cudaEvent_t base_ready[2] = {nullptr, nullptr}, slot_free[2] = {nullptr, nullptr};
+    int slot = 0;
+    int64_t launches = 0;
+    int num_sms = 148;
+    // live profiling: event pairs around launches, resolved by ffnrm_profile_read
+    bool prof = false;
+    std::vector<cudaEvent_t> prof_pool;
+    size_t prof_used = 0;
+    std::vector<int> prof_kind;
+    double prof_ms[3] = {0, 0, 0};
+    int64_t prof_count[3] = {0, 0, 0};
+};
+
+namespace {
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+int dev_alloc(DevBuf &b, size_t bytes) {
+    if (bytes == 0) return FFNRM_OK;
+    if (cudaMalloc(&b.ptr, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(FFNRM_ERR_NOMEM, "cudaMalloc of %zu bytes failed", bytes);
+    }
+    b.bytes = bytes;
+    return FFNRM_OK;
+}
+
+void dev_free(DevBuf &b) {
+    if (b.ptr) cudaFree(b.ptr);
+    b.ptr = nullptr;
+    b.bytes = 0;
+}
+
+int upload(DevBuf &b, const void *host, size_t bytes) {
+    int rc = dev_alloc(b, bytes);
+    if (rc) return rc;
+    FFNRM_CUDA(cudaMemcpy(b.ptr, host, bytes, cudaMemcpyHostToDevice));
+    return FFNRM_OK;
+}
+
+// Row-pack codes [F, D] (values 0..3 after shifting) into the pair layout.
+void pack_pair(const uint8_t *q, int shift, int64_t F, int64_t D, std::vector<uint8_t> &out) {
+    out.assign(size_t(F * D / 4), 0);
+    for (int64_t r = 0; r < F; ++r) {
+        const uint8_t *src = q + r * D;
+        uint8_t *dst = out.data() + r * (D / 4);
+        for (int64_t j = 0; j < D / 4; ++j) {
+            uint8_t v = 0;
+            for (int i = 0; i < 4; ++i) v |= uint8_t(((src[4 * j + i] >> shift) & 3) << (2 * i));
+            dst[j] = v;
+        }
+    }
+}
+
+// Row-pack bit `bit` of codes [F, D] into the plane layout.
+void pack_plane(const uint8_t *q, int bit, int64_t F, int64_t D, std::vector<uint8_t> &out) {
+    out.assign(size_t(F * D / 8), 0);
+    for (int64_t r = 0; r < F; ++r) {
+        const uint8_t *src = q + r * D;
+        uint8_t *dst = out.data() + r * (D / 8);
+        for (int64_t j = 0; j < D / 8; ++j) {
+            uint8_t v = 0;
+            for (int i = 0; i < 8; ++i) v |= uint8_t(((src[8 * j + i] >> bit) & 1) << i);
+            dst[j] = v;
+        }
+    }
+}
+
+// Decode one projection's input codes into full / low code bytes [F, D].
+// Returns in `lo` the r-bit low codes and, when high codes are available, in `full` the
+// complete Q4 codes (`have_full` = true).
+int decode_codes(const ffnrm_layer_weights *w, const uint8_t *codes, const uint8_t *high, int r, int64_t F,
+                 int64_t D, std::vector<uint8_t> &lo, std::vector<uint8_t> &full, bool &have_full) {
+    const int64_t n = F * D;
+    lo.resize(size_t(n));
+    have_full = false;
+    const uint8_t mask = uint8_t((1 << r) - 1);
+    if (w->codes_format == FFNRM_CODES_Q4_BYTES) {
+        for (int64_t i = 0; i < n; ++i) {
+            if (codes[i] > 15) return fail(FFNRM_ERR_ARG, "Q4 codes must be in [0, 15]");
+            lo[size_t(i)] = codes[i] & mask;
+        }
+        if (w->keep_fallback) {
+            full.assign(codes, codes + n);
+            have_full = true;
+        }
+        return FFNRM_OK;
+    }
+    if (w->codes_format == FFNRM_CODES_QLO2_ROWPACKED) {
+        if (r != 2) return fail(FFNRM_ERR_ARG, "QLO2 row-packed codes require residual_bits == 2");
+        for (int64_t i = 0; i < n; ++i) lo[size_t(i)] = (codes[i / 4] >> (2 * (i & 3))) & 3;
+    } else if (w->codes_format == FFNRM_CODES_BITPLANES) {
+        const int64_t plane = n / 8;
+        for (int64_t i = 0; i < n; ++i) {
+            uint8_t v = 0;
+            for (int b = 0; b < r; ++b) v |= uint8_t(((codes[b * plane + i / 8] >> (i & 7)) & 1) << b);
+            lo[size_t(i)] = v;
+        }
+    } else {
+        return fail(FFNRM_ERR_ARG, "unknown codes_format %d", w->codes_format);
+    }
+    if (high) {
+        const int64_t plane = n / 8;
+        const int hb = 4 - r;
+        full.resize(size_t(n));
+        for (int64_t i = 0; i < n; ++i) {
+            uint8_t v = 0;
+            for (int b = 0; b < hb; ++b) v |= uint8_t(((high[b * plane + i / 8] >> (i & 7)) & 1) << b);
+            full[size_t(i)] = uint8_t((v << r) | lo[size_t(i)]);
+        }
+        have_full = true;
+    }
+    return FFNRM_OK;
+}
+
+bool all_half_exact(const float *v, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) {
+        const float back = __half2float(__float2half_rn(v[i]));
+        if (!(back == v[i]) && !(std::isnan(v[i]) && std::isnan(back))) return false;
+    }
+    return true;
+}
+
+int upload_scales(DevBuf &b, const float *v, int64_t n, bool as_half) {
+    if (!as_half) return upload(b, v, size_t(n) * 4);
+    std::vector<__half> h{};
+    h.resize(size_t(n));
+    for (int64_t i = 0; i < n; ++i) h[size_t(i)] = __float2half_rn(v[i]);
+    return upload(b, h.data(), size_t(n) * 2);
+}
+
+void free_layer(LayerDev &L) {
+    for (int p = 0; p < 2; ++p) {
+        dev_free(L.pair[p]);
+        dev_free(L.plane[p]);
+        dev_free(L.pair_hi[p]);
+        dev_free(L.alpha[p]);
+        dev_free(L.beta[p]);
+    }
+    dev_free(L.down);
+    L.loaded = false;
+}
+
+int check_ctx(ffnrm_ctx *ctx, int layer) {
+    if (!ctx) return fail(FFNRM_ERR_ARG, "null context");
+    if (layer < 0 || layer >= ctx->cfg.n_layers) return fail(FFNRM_ERR_ARG, "layer %d out of range [0, %d)", layer, ctx->cfg.n_layers);
+    if (!ctx->layers[size_t(layer)].loaded) return fail(FFNRM_ERR_STATE, "layer %d is not loaded", layer);
+    return FFNRM_OK;
+}
+
+int check_tokens(ffnrm_ctx *ctx, int tokens) {
+    if (tokens < 1 || tokens > ctx->cfg.max_tokens)
+        return fail(FFNRM_ERR_ARG, "tokens=%d outside [1, max_tokens=%d]", tokens, ctx->cfg.max_tokens);
+    return FFNRM_OK;
+}
+
+cudaEvent_t prof_event(ffnrm_ctx *ctx) {
+    if (ctx->prof_used == ctx->prof_pool.size()) {
+        cudaEvent_t e = nullptr;
+        if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+        ctx->prof_pool.push_back(e);
+    }
+    return ctx->prof_pool[ctx->prof_used++];
+}
+
+// Brackets one kernel launch with events when profiling is on.
+struct ProfScope {
+    ffnrm_ctx *ctx;
+    cudaStream_t st;
+    int kind;
+    bool on;
+    ProfScope(ffnrm_ctx *c, cudaStream_t s, int k) : ctx(c), st(s), kind(k), on(c->prof) {
+        if (on) {
+            cudaEvent_t e = prof_event(ctx);
+            if (!e) { on = false; return; }
+            cudaEventRecord(e, st);
+        }
+    }
+    ~ProfScope() {
+        if (!on) return;
+        cudaEvent_t e = prof_event(ctx);
+        if (!e) { ctx->prof_used--; return; }
+        cudaEventRecord(e, st);
+        ctx->prof_kind.push_back(kind);
+    }
+};
+
+// ---------------------------------------------------------------------------
+// Kernel launchers
+// ---------------------------------------------------------------------------
+template <int RB, int TT, int R, bool AH>
+int launch_residual_t(ffnrm_ctx *ctx, ffnrm::ResidualParams &p, cudaStream_t st) {
+    const size_t smem = ffnrm::residual_smem_bytes(TT, p.G, p.need_pair, p.need_plane);
+    auto kern = ffnrm::residual_dp4a_kernel<RB, TT, R, AH>;
+    if (smem > 48 * 1024) FFNRM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+    const int rows_per_cta = 8 * R;
+    p.row_blocks = (p.F + rows_per_cta - 1) / rows_per_cta;
+    dim3 grid(unsigned(2 * p.row_blocks), unsigned((p.T + TT - 1) / TT));
+    ProfScope prof(ctx, st, FFNRM_KERNEL_RESIDUAL);
+    kern<<<grid, 256, smem, st>>>(p);
+    ctx->launches++;
+    FFNRM_CUDA(cudaGetLastError());
+    return FFNRM_OK;
+}
+
+template <int RB, int TT>
+int launch_residual_tt(ffnrm_ctx *ctx, ffnrm::ResidualParams &p, bool half, cudaStream_t st) {
+    constexpr int R = RB == 3 ? 2 : 4;
+    return half ? launch_residual_t<RB, TT, R, true>(ctx, p, st) : launch_residual_t<RB, TT, R, false>(ctx, p, st);
+}
+
+template <int RB>
+int launch_residual_rb(ffnrm_ctx *ctx, ffnrm::ResidualParams &p, bool half, cudaStream_t st) {
+    if (p.T == 1) return launch_residual_tt<RB, 1>(ctx, p, half, st);
+    if (p.T == 2) return launch_residual_tt<RB, 2>(ctx, p, half, st);
+    return launch_residual_tt<RB, 4>(ctx, p, half, st);
+}
+
+int enqueue_residual(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s, int T, float *gate_res,
+                     float *up_res, int32_t *dots, const uint8_t *tiles, cudaStream_t st) {
+    LayerDev &L = ctx->layers[size_t(layer)];
+    if (tiles && !L.has_fallback)
+        return fail(FFNRM_ERR_STATE, "fallback tiles given but layer %d was loaded without fallback data", layer);
+    ffnrm::ResidualParams p{};
+    for (int q = 0; q < 2; ++q)
+        p.proj[q] = ffnrm::ProjView{static_cast<const uint8_t *>(L.pair[q].ptr), static_cast<const uint8_t *>(L.plane[q].ptr),
+                                    static_cast<const uint8_t *>(L.pair_hi[q].ptr), L.alpha[q].ptr, L.beta[q].ptr};
+    p.z = z;
+    p.s = s;
+    p.out[0] = gate_res;
+    p.out[1] = up_res;
+    p.dots = dots;
+    p.fallback_tiles = tiles;
+    p.F = ctx->cfg.d_ff;
+    p.D = ctx->cfg.d_model;
+    p.G = ctx->G;
+    p.T = T;
+    p.tile_rows = ctx->cfg.base_tile_rows;
+    const int r = ctx->cfg.residual_bits;
+    p.need_pair = (r != 1) || tiles != nullptr;
+    p.need_plane = r != 2;
+    switch (r) {
+        case 1: return launch_residual_rb<1>(ctx, p, L.scales_half, st);
+        case 2: return launch_residual_rb<2>(ctx, p, L.scales_half, st);
+        default: return launch_residual_rb<3>(ctx, p, L.scales_half, st);
+    }
+}
+
+int enqueue_down(ffnrm_ctx *ctx, int layer, int T, const float *gate_base, const float *up_base,
+                 const uint8_t *tiles, float *y32, uint16_t *y16, cudaStream_t st) {
+    LayerDev &L = ctx->layers[size_t(layer)];
+    const int F = ctx->cfg.d_ff, D = ctx->cfg.d_model;
+    ffnrm::DownParams p{};
+    p.gate_res = ctx->res[0];
+    p.up_res = ctx->res[1];
+    p.gate_base = gate_base;
+    p.up_base = up_base;
+    p.fallback_tiles = tiles;
+    p.down = static_cast<const __half *>(L.down.ptr);
+    p.partial = ctx->partial;
+    p.F = F;
+    p.D = D;
+    p.T = T;
+    p.tile_rows = ctx->cfg.base_tile_rows;
+    const int otiles = D / ffnrm::kDownTileRows;
+    int splits = std::max(1, std::min(ctx->max_splits, (2 * ctx->num_sms + otiles - 1) / otiles));
+    int kc = (F + splits - 1) / splits;
+    kc = (kc + 7) / 8 * 8;
+    splits = (F + kc - 1) / kc;
+    p.splits = splits;
+    p.kc = kc;
+    const int TT = T == 1 ? 1 : (T == 2 ? 2 : 4);
+    const size_t smem = size_t(TT) * kc * sizeof(float);
+    dim3 grid(unsigned(otiles), unsigned(splits), unsigned((T + TT - 1) / TT));
+    auto run = [&](auto kern) -> int {
+        if (smem > 48 * 1024) FFNRM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+        ProfScope prof(ctx, st, FFNRM_KERNEL_DOWN);
+        kern<<<grid, 256, smem, st>>>(p);
+        ctx->launches++;
+        FFNRM_CUDA(cudaGetLastError());
+        return FFNRM_OK;
+    };
+    int rc = TT == 1 ? run(ffnrm::swiglu_down_kernel<1>) : (TT == 2 ? run(ffnrm::swiglu_down_kernel<2>) : run(ffnrm::swiglu_down_kernel<4>));
+    if (rc) return rc;
+    const int64_t n = int64_t(T) * D;
+    const int blocks = int(std::min<int64_t>((n + 255) / 256, 4 * ctx->num_sms));
+    {
+        ProfScope prof(ctx, st, FFNRM_KERNEL_REDUCE);
+        ffnrm::splitk_reduce_kernel<<<blocks, 256, 0, st>>>(ctx->partial, splits, n, y32, reinterpret_cast<__half *>(y16));
+    }
+    ctx->launches++;
+    FFNRM_CUDA(cudaGetLastError());
+    return FFNRM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *ffnrm_last_error(void) { return g_last_error.c_str(); }
+const char *ffnrm_version(void) { return "ffnrm 0.1 (sm_100a)"; }
+
+int ffnrm_create(ffnrm_ctx **out, int device, const ffnrm_config *cfg) {
+    if (!out || !cfg) return fail(FFNRM_ERR_ARG, "null argument");
+    *out = nullptr;
+    const ffnrm_config c = *cfg;
+    if (c.d_model <= 0 || c.d_model % 256) return fail(FFNRM_ERR_ARG, "d_model=%d must be a positive multiple of 256", c.d_model);
+    if (c.d_ff <= 0 || c.d_ff % 8) return fail(FFNRM_ERR_ARG, "d_ff=%d must be a positive multiple of 8", c.d_ff);
+    if (c.residual_bits < 1 || c.residual_bits > 3) return fail(FFNRM_ERR_ARG, "residual_bits=%d must be 1, 2 or 3", c.residual_bits);
+    if (c.n_layers <= 0 || c.max_tokens <= 0) return fail(FFNRM_ERR_ARG, "n_layers and max_tokens must be positive");
+    if (c.base_tile_rows <= 0) return fail(FFNRM_ERR_ARG, "base_tile_rows must be positive");
+    int count = 0;
+    FFNRM_CUDA(cudaGetDeviceCount(&count));
+    if (device < 0 || device >= count) return fail(FFNRM_ERR_ARG, "device %d not present (%d devices)", device, count);
+    DeviceGuard guard(device);
+    auto *ctx = new (std::nothrow) ffnrm_ctx;
+    if (!ctx) return fail(FFNRM_ERR_NOMEM, "host allocation failed");
+    ctx->device = device;
+    ctx->cfg = c;
+    ctx->G = c.d_model / 32;
+    ctx->layers.resize(size_t(c.n_layers));
+    cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
+    const size_t TF = size_t(c.max_tokens) * c.d_ff, TD = size_t(c.max_tokens) * c.d_model;
+    const int ntiles = (c.d_ff + c.base_tile_rows - 1) / c.base_tile_rows;
+    bool ok = cudaMalloc(&ctx->res[0], TF * 4) == cudaSuccess && cudaMalloc(&ctx->res[1], TF * 4) == cudaSuccess &&
+              cudaMalloc(&ctx->partial, size_t(ctx->max_splits) * TD * 4) == cudaSuccess &&
+              cudaMalloc(&ctx->z_dev, TD) == cudaSuccess &&
+              cudaMalloc(&ctx->s_dev, size_t(c.max_tokens) * ctx->G * 4) == cudaSuccess &&
+              cudaMalloc(&ctx->y16_dev, TD * 2) == cudaSuccess;
+    for (int sl = 0; sl < 2 && ok; ++sl) {
+        ok = cudaMalloc(&ctx->base_dev[sl][0], TF * 4) == cudaSuccess && cudaMalloc(&ctx->base_dev[sl][1], TF * 4) == cudaSuccess &&
+             cudaMalloc(&ctx->tiles_dev[sl], size_t(ntiles)) == cudaSuccess;
+    }
+    ok = ok && cudaStreamCreateWithFlags(&ctx->copy_stream, cudaStreamNonBlocking) == cudaSuccess;
+    for (int sl = 0; sl < 2 && ok; ++sl)
+        ok = cudaEventCreateWithFlags(&ctx->base_ready[sl], cudaEventDisableTiming) == cudaSuccess &&
+             cudaEventCreateWithFlags(&ctx->slot_free[sl], cudaEventDisableTiming) == cudaSuccess;
+    if (!ok) {
+        cudaGetLastError();
+        ffnrm_destroy(ctx);
+        return fail(FFNRM_ERR_NOMEM, "workspace allocation failed (max_tokens=%d, d_ff=%d)", c.max_tokens, c.d_ff);
+    }
+    *out = ctx;
+    return FFNRM_OK;
+}
+
+int ffnrm_destroy(ffnrm_ctx *ctx) {
+    if (!ctx) return FFNRM_OK;
+    DeviceGuard guard(ctx->device);
+    cudaDeviceSynchronize();
+    for (auto &L : ctx->layers) free_layer(L);
+    cudaFree(ctx->res[0]);
+    cudaFree(ctx->res[1]);
+    cudaFree(ctx->partial);
+    cudaFree(ctx->z_dev);
+    cudaFree(ctx->s_dev);
+    cudaFree(ctx->y16_dev);
+    for (int sl = 0; sl < 2; ++sl) {
+        cudaFree(ctx->base_dev[sl][0]);
+        cudaFree(ctx->base_dev[sl][1]);
+        cudaFree(ctx->tiles_dev[sl]);
+        if (ctx->base_ready[sl]) cudaEventDestroy(ctx->base_ready[sl]);
+        if (ctx->slot_free[sl]) cudaEventDestroy(ctx->slot_free[sl]);
+    }
+    if (ctx->copy_stream) cudaStreamDestroy(ctx->copy_stream);
+    for (cudaEvent_t e : ctx->prof_pool) cudaEventDestroy(e);
+    delete ctx;
+    return FFNRM_OK;
+}
+
+int ffnrm_load_layer(ffnrm_ctx *ctx, int layer, const ffnrm_layer_weights *w) {
+    if (!ctx || !w) return fail(FFNRM_ERR_ARG, "null argument");
+    if (layer < 0 || layer >= ctx->cfg.n_layers) return fail(FFNRM_ERR_ARG, "layer %d out of range", layer);
+    if (!w->gate_codes || !w->up_codes || !w->gate_alpha || !w->up_alpha || !w->down)
+        return fail(FFNRM_ERR_ARG, "codes, alpha and down are required");
+    const int64_t F = ctx->cfg.d_ff, D = ctx->cfg.d_model, G = ctx->G;
+    const int r = ctx->cfg.residual_bits;
+    if (w->down_ld < F) return fail(FFNRM_ERR_ARG, "down_ld=%lld must be >= d_ff=%lld", (long long)w->down_ld, (long long)F);
+    DeviceGuard guard(ctx->device);
+    LayerDev &L = ctx->layers[size_t(layer)];
+    free_layer(L);
+    const bool want_hi = w->codes_format == FFNRM_CODES_Q4_BYTES ? w->keep_fallback != 0 : (w->gate_high && w->up_high);
+    const bool have_beta = w->gate_beta && w->up_beta;
+    L.has_fallback = want_hi && have_beta;
+    if (want_hi && !have_beta) return fail(FFNRM_ERR_ARG, "fallback high codes need gate_beta and up_beta");
+    L.scales_half = all_half_exact(w->gate_alpha, F * G) && all_half_exact(w->up_alpha, F * G) &&
+                    (!L.has_fallback || (all_half_exact(w->gate_beta, F * G) && all_half_exact(w->up_beta, F * G)));
+    const uint8_t *codes[2] = {w->gate_codes, w->up_codes};
+    const uint8_t *high[2] = {w->gate_high, w->up_high};
+    const float *alpha[2] = {w->gate_alpha, w->up_alpha};
+    const float *beta[2] = {w->gate_beta, w->up_beta};
+    std::vector<uint8_t> lo, full, packed;
+    int rc = FFNRM_OK;
+    for (int q = 0; q < 2 && rc == FFNRM_OK; ++q) {
+        bool have_full = false;
+        rc = decode_codes(w, codes[q], L.has_fallback ? high[q] : nullptr, r, F, D, lo, full, have_full);
+        if (rc) break;
+        if (r != 1 || L.has_fallback) {
+            // bits 0-1 of the full code equal the low two residual bits for r >= 2
+            pack_pair(have_full ? full.data() : lo.data(), 0, F, D, packed);
+            if ((rc = upload(L.pair[q], packed.data(), packed.size()))) break;
+        }
+        if (r != 2) {
+            pack_plane(lo.data(), r == 1 ? 0 : 2, F, D, packed);
+            if ((rc = upload(L.plane[q], packed.data(), packed.size()))) break;
+        }
+        if (L.has_fallback) {
+            pack_pair(full.data(), 2, F, D, packed);
+            if ((rc = upload(L.pair_hi[q], packed.data(), packed.size()))) break;
+            if ((rc = upload_scales(L.beta[q], beta[q], F * G, L.scales_half))) break;
+        }
+        rc = upload_scales(L.alpha[q], alpha[q], F * G, L.scales_half);
+    }
+    if (rc == FFNRM_OK) {
+        rc = dev_alloc(L.down, size_t(D * F * 2));
+        if (rc == FFNRM_OK) {
+            cudaError_t e = cudaMemcpy2D(L.down.ptr, size_t(F) * 2, w->down, size_t(w->down_ld) * 2, size_t(F) * 2,
+                                         size_t(D), cudaMemcpyHostToDevice);
+            if (e != cudaSuccess) rc = fail(FFNRM_ERR_CUDA, "down upload failed: %s", cudaGetErrorString(e));
+        }
+    }
+    if (rc) {
+        free_layer(L);
+        return rc;
+    }
+    L.loaded = true;
+    return FFNRM_OK;
+}
+
+int ffnrm_residual(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s, int tokens, float *gate_res,
+                   float *up_res, int32_t *group_dots, const uint8_t *fallback_tiles, void *stream) {
+    int rc = check_ctx(ctx, layer);
+    if (rc) return rc;
+    if ((rc = check_tokens(ctx, tokens))) return rc;
+    if (!z || !s || !gate_res || !up_res) return fail(FFNRM_ERR_ARG, "null device pointer");
+    DeviceGuard guard(ctx->device);
+    return enqueue_residual(ctx, layer, z, s, tokens, gate_res, up_res, group_dots, fallback_tiles,
+                            static_cast<cudaStream_t>(stream));
+}
+
+int ffnrm_ffn_forward(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s, int tokens, const float *gate_base,
+                      const float *up_base, const uint8_t *fallback_tiles, float *y_f32, uint16_t *y_f16,
+                      void *stream) {
+    int rc = check_ctx(ctx, layer);
+    if (rc) return rc;
+    if ((rc = check_tokens(ctx, tokens))) return rc;
+    if (!z || !s || !gate_base || !up_base) return fail(FFNRM_ERR_ARG, "null device pointer");
+    if (!y_f32 && !y_f16) return fail(FFNRM_ERR_ARG, "no output requested");
+    DeviceGuard guard(ctx->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if ((rc = enqueue_residual(ctx, layer, z, s, tokens, ctx->res[0], ctx->res[1], nullptr, fallback_tiles, st))) return rc;
+    return enqueue_down(ctx, layer, tokens, gate_base, up_base, fallback_tiles, y_f32, y_f16, st);
+}
+
+int ffnrm_ffn_forward_host(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s, int tokens,
+                           const float *gate_base, const float *up_base, const uint8_t *fallback_tiles,
+                           uint16_t *y_f16, void *stream) {
+    int rc = check_ctx(ctx, layer);
+    if (rc) return rc;
+    if ((rc = check_tokens(ctx, tokens))) return rc;
+    if (!z || !s || !gate_base || !up_base || !y_f16) return fail(FFNRM_ERR_ARG, "null host pointer");
+    DeviceGuard guard(ctx->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int F = ctx->cfg.d_ff, D = ctx->cfg.d_model, G = ctx->G;
+    const int sl = ctx->slot;
+    ctx->slot ^= 1;
+    const size_t tf_bytes = size_t(tokens) * F * 4;
+    // Activations on the compute stream (needed first by the residual contraction).
+    FFNRM_CUDA(cudaMemcpyAsync(ctx->z_dev, z, size_t(tokens) * D, cudaMemcpyHostToDevice, st));
+    FFNRM_CUDA(cudaMemcpyAsync(ctx->s_dev, s, size_t(tokens) * G * 4, cudaMemcpyHostToDevice, st));
+    const uint8_t *tiles_dev = nullptr;
+    if (fallback_tiles) {
+        const int ntiles = (F + ctx->cfg.base_tile_rows - 1) / ctx->cfg.base_tile_rows;
+        FFNRM_CUDA(cudaMemcpyAsync(ctx->tiles_dev[sl], fallback_tiles, size_t(ntiles), cudaMemcpyHostToDevice, st));
+        tiles_dev = ctx->tiles_dev[sl];
+    }
+    // Base sums on the copy stream, into a slot no earlier call is still reading.
+    FFNRM_CUDA(cudaStreamWaitEvent(ctx->copy_stream, ctx->slot_free[sl], 0));
+    FFNRM_CUDA(cudaMemcpyAsync(ctx->base_dev[sl][0], gate_base, tf_bytes, cudaMemcpyHostToDevice, ctx->copy_stream));
+    FFNRM_CUDA(cudaMemcpyAsync(ctx->base_dev[sl][1], up_base, tf_bytes, cudaMemcpyHostToDevice, ctx->copy_stream));
+    FFNRM_CUDA(cudaEventRecord(ctx->base_ready[sl], ctx->copy_stream));
+    if ((rc = enqueue_residual(ctx, layer, ctx->z_dev, ctx->s_dev, tokens, ctx->res[0], ctx->res[1], nullptr, tiles_dev, st)))
+        return rc;
+    FFNRM_CUDA(cudaStreamWaitEvent(st, ctx->base_ready[sl], 0));
+    if ((rc = enqueue_down(ctx, layer, tokens, ctx->base_dev[sl][0], ctx->base_dev[sl][1], tiles_dev, nullptr,
+                           ctx->y16_dev, st)))
+        return rc;
+    FFNRM_CUDA(cudaEventRecord(ctx->slot_free[sl], st));
+    FFNRM_CUDA(cudaMemcpyAsync(y_f16, ctx->y16_dev, size_t(tokens) * D * 2, cudaMemcpyDeviceToHost, st));
+    return FFNRM_OK;
+}
+
+int ffnrm_host_register(void *ptr, size_t bytes) {
+    if (!ptr || !bytes) return fail(FFNRM_ERR_ARG, "null or empty range");
+    FFNRM_CUDA(cudaHostRegister(ptr, bytes, cudaHostRegisterPortable));
+    return FFNRM_OK;
+}
+
+int ffnrm_host_unregister(void *ptr) {
+    FFNRM_CUDA(cudaHostUnregister(ptr));
+    return FFNRM_OK;
+}
+
+int ffnrm_cast_f16(const float *src, uint16_t *dst, int64_t n, void *stream) {
+    if (!src || !dst || n < 0) return fail(FFNRM_ERR_ARG, "bad cast arguments");
+    if (n == 0) return FFNRM_OK;
+    const int blocks = int(std::min<int64_t>((n + 255) / 256, 1024));
+    ffnrm::cast_f16_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(src, reinterpret_cast<__half *>(dst), n);
+    FFNRM_CUDA(cudaGetLastError());
+    return FFNRM_OK;
+}
+
+int ffnrm_layer_bytes(ffnrm_ctx *ctx, int layer, int64_t *residual_bytes, int64_t *down_bytes) {
+    int rc = check_ctx(ctx, layer);
+    if (rc) return rc;
+    const LayerDev &L = ctx->layers[size_t(layer)];
+    int64_t res = 0;
+    for (int q = 0; q < 2; ++q) res += int64_t(L.alpha[q].bytes);
+    const int r = ctx->cfg.residual_bits;
+    for (int q = 0; q < 2; ++q) {
+        if (r != 1) res += int64_t(L.pair[q].bytes);
+        if (r != 2) res += int64_t(L.plane[q].bytes);
+    }
+    if (residual_bytes) *residual_bytes = res;
+    if (down_bytes) *down_bytes = int64_t(L.down.bytes);
+    return FFNRM_OK;
+}
+
+int64_t ffnrm_launch_count(ffnrm_ctx *ctx) { return ctx ? ctx->launches : -1; }
+
+int ffnrm_profile_enable(ffnrm_ctx *ctx, int enable) {
+    if (!ctx) return fail(FFNRM_ERR_ARG, "null context");
+    DeviceGuard guard(ctx->device);
+    if (ctx->prof_used) FFNRM_CUDA(cudaDeviceSynchronize());
+    ctx->prof = enable != 0;
+    ctx->prof_used = 0;
+    ctx->prof_kind.clear();
+    for (int k = 0; k < 3; ++k) ctx->prof_ms[k] = 0, ctx->prof_count[k] = 0;
+    return FFNRM_OK;
+}
+
+int ffnrm_profile_read(ffnrm_ctx *ctx, int kind, double *total_ms, int64_t *launches) {
+    if (!ctx || kind < 0 || kind > 2) return fail(FFNRM_ERR_ARG, "bad profile arguments");
+    DeviceGuard guard(ctx->device);
+    for (size_t i = 0; i < ctx->prof_kind.size(); ++i) {
+        cudaEvent_t a = ctx->prof_pool[2 * i], b = ctx->prof_pool[2 * i + 1];
+        FFNRM_CUDA(cudaEventSynchronize(b));
+        float ms = 0.f;
+        FFNRM_CUDA(cudaEventElapsedTime(&ms, a, b));
+        ctx->prof_ms[ctx->prof_kind[i]] += ms;
+        ctx->prof_count[ctx->prof_kind[i]] += 1;
+    }
+    ctx->prof_kind.clear();
+    ctx->prof_used = 0;
+    if (total_ms) *total_ms = ctx->prof_ms[kind];
+    if (launches) *launches = ctx->prof_count[kind];
+    return FFNRM_OK;
+}
+
+}  // extern "C"

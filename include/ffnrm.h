@@ -1,0 +1,163 @@
+/*
+ * ffnrm.h — C ABI of the B200 exact integer-domain gated-FFN base/residual split.
+ *
+ * The path: every Q4 weight code is split exactly as q = 2^r * q_hi + q_lo. The host
+ * supplies the "base" partial sums  s*(alpha*2^r*dot(q_hi, z) + beta*sum(z))  per
+ * token and d_ff row; the GPU computes the "residual"  s*alpha*dot(q_lo, z)  from
+ * exact int32 group dots, merges g = g_base + g_res and u = u_base + u_res before
+ * SiLU(g)*u, and runs the fp16 down projection.
+ *
+ * The reference ships this path as three standalone CUDA runners and Python/Triton
+ * twins, with no library ABI. Each entry point below names the reference code it
+ * replaces (paths relative to the reference project root).
+ *
+ * Conventions
+ *   - Plain pointers and sizes only. "device" pointers are CUDA device addresses
+ *     on the context's device; "host" pointers are ordinary (preferably pinned)
+ *     host memory. `stream` is a cudaStream_t passed as void* (NULL = legacy
+ *     default stream). All compute calls are stream-ordered and asynchronous.
+ *   - Shapes: T tokens, D = d_model (reference "hidden"), F = d_ff rows held by
+ *     this context (a shard of the full d_ff in multi-GPU runs), G = D/32.
+ *     Activations z are int8 [T, D] row-major, their per-group scales s are
+ *     f32 [T, G]; base sums and residual outputs are f32 [T, F]; y is [T, D].
+ *   - Return value: FFNRM_OK or an error code; ffnrm_last_error() gives the
+ *     message of the last failing call on the calling thread. Argument errors
+ *     correspond to the reference's ValueError / `error: ...` exit 1 paths.
+ *   - One context per device per host thread at a time; contexts are not
+ *     internally locked.
+ */
+#ifndef FFNRM_H
+#define FFNRM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FFNRM_OK 0
+#define FFNRM_ERR_ARG 1     /* shape / argument error (reference: ValueError) */
+#define FFNRM_ERR_CUDA 2    /* CUDA runtime error */
+#define FFNRM_ERR_STATE 3   /* e.g. layer not loaded, fallback data missing */
+#define FFNRM_ERR_NOMEM 4   /* device or pinned allocation failed */
+
+/* Residual code formats accepted by ffnrm_load_layer. */
+#define FFNRM_CODES_Q4_BYTES 0       /* full Q4 codes, one byte per code [F, D], values 0..15 */
+#define FFNRM_CODES_QLO2_ROWPACKED 1 /* r = 2 low codes, row-packed [F, D/4]
+                                        (scripts/export_cuda_residual_artifact_v2.py:13-24) */
+#define FFNRM_CODES_BITPLANES 2      /* r low-code bit planes, plane-major, each F*D/8 bytes
+                                        (scripts/compile_q4k_host_base_gpu_residual.py:17-26) */
+
+typedef struct ffnrm_ctx ffnrm_ctx;
+
+typedef struct {
+    int32_t d_model;        /* D, a multiple of 256 (Q4_K super-block) */
+    int32_t d_ff;           /* F rows held by this context, a multiple of 8 */
+    int32_t residual_bits;  /* r in {1, 2, 3} */
+    int32_t n_layers;       /* layers this context can hold */
+    int32_t max_tokens;     /* largest T of any call (sizes the workspace) */
+    int32_t base_tile_rows; /* rows per base tile / fallback tile (reference TILE_ROWS) */
+} ffnrm_config;
+
+typedef struct {
+    int32_t codes_format;          /* FFNRM_CODES_* */
+    const uint8_t *gate_codes;     /* Q4_BYTES: full codes; otherwise the residual low codes */
+    const uint8_t *up_codes;
+    const uint8_t *gate_high;      /* BITPLANES / QLO2: optional (4-r) high-code bit planes
+                                      (compile_q4k_host_base_gpu_residual.py:66); NULL = no fallback */
+    const uint8_t *up_high;
+    const float *gate_alpha;       /* [F, G] per-group weight scale */
+    const float *up_alpha;
+    const float *gate_beta;        /* [F, G] per-group weight min term; NULL = no fallback */
+    const float *up_beta;
+    const uint16_t *down;          /* fp16 down weight, row o at down + o*down_ld, F columns */
+    int64_t down_ld;               /* leading dimension of `down` in elements (>= F) */
+    int32_t keep_fallback;         /* Q4_BYTES only: also keep the high codes for fallback tiles */
+} ffnrm_layer_weights;
+
+/* Create a context on `device`. Replaces the per-runner setup of
+ * src/exact_cpu_base_gpu_full_ffn_runner.cu:375-397 (device buffers, streams). */
+int ffnrm_create(ffnrm_ctx **out, int device, const ffnrm_config *cfg);
+int ffnrm_destroy(ffnrm_ctx *ctx);
+
+/* Copy one layer's weights (host pointers, borrowed for the call) into HBM.
+ * Replaces load_projection (src/exact_residual_cuda_runner.cu:88-120) and the
+ * resident fp16 down upload (src/exact_cpu_base_gpu_full_ffn_runner.cu:375-387).
+ * alpha/beta are kept as fp16 on the device when every value is fp16-exact
+ * (lossless), else as f32. */
+int ffnrm_load_layer(ffnrm_ctx *ctx, int layer, const ffnrm_layer_weights *w);
+
+/* Residual gate/up contraction. Replaces residual_kernel
+ * (src/exact_residual_cuda_runner.cu:122-159, and its copies in
+ * exact_main_residual_cuda_runner.cu:213-233 and
+ * exact_cpu_base_gpu_full_ffn_runner.cu:195-215) for both projections in one launch.
+ * Device pointers: z [T,D] i8, s [T,G] f32, gate_res/up_res [T,F] f32.
+ * group_dots (optional, device, NULL to skip): [2, T, F, G] int32, the exact
+ * residual group dots sum_i q_lo*z (gate then up).
+ * fallback_tiles (optional, device): rows of flagged tiles receive the unsplit
+ * exact projection sum_g s*(alpha*dot(q,z) + beta*sum(z)) instead of the residual
+ * (the "center-GPU exact FFN" fallback, src/phone_ffn_loopback.py:155-197). */
+int ffnrm_residual(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s, int tokens,
+                   float *gate_res, float *up_res, int32_t *group_dots, const uint8_t *fallback_tiles,
+                   void *stream);
+
+/* Full split FFN, HBM-resident base mode. Replaces enqueue_tile + swiglu_down_kernel
+ * (src/exact_cpu_base_gpu_full_ffn_runner.cu:217-289) and the validated Python
+ * chain (scripts/benchmark_cpu_base_gpu_full_ffn.py:228-337).
+ * Device pointers: z, s as above; gate_base/up_base [T,F] f32; fallback_tiles
+ * (device, optional) one byte per base tile, nonzero = recompute those rows on
+ * the unsplit exact path (needs fallback data loaded; the base of those rows is
+ * ignored); y_f32 (optional) [T,D] f32 partial sum over this context's rows;
+ * y_f16 (optional) [T,D] fp16. */
+int ffnrm_ffn_forward(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s, int tokens,
+                      const float *gate_base, const float *up_base, const uint8_t *fallback_tiles,
+                      float *y_f32, uint16_t *y_f16, void *stream);
+
+/* Full split FFN, host-streamed base mode (the end-to-end call). All data
+ * pointers are HOST pointers (pinned for full overlap): z [T,D], s [T,G],
+ * gate_base/up_base [T,F], fallback_tiles (optional) [ceil(F/base_tile_rows)],
+ * y_f16 [T,D]. z and s are uploaded on `stream`; the base sums are uploaded on the
+ * context's copy stream into one of two device slots (alternating per call, so the
+ * upload for the next layer overlaps this layer's kernels) while the residual
+ * contraction runs on `stream`; the merge waits for the upload by event. This is
+ * the double-buffered copy/compute pipeline of
+ * src/exact_cpu_base_gpu_full_ffn_runner.cu:315-345, with one transfer per
+ * projection instead of one per tile because the base arrives complete. y is
+ * copied back on `stream`. Host buffers must stay valid until `stream` completes. */
+int ffnrm_ffn_forward_host(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s, int tokens,
+                           const float *gate_base, const float *up_base, const uint8_t *fallback_tiles,
+                           uint16_t *y_f16, void *stream);
+
+/* Page-lock an existing host range for async copies (cudaHostRegister) and undo it.
+ * Replaces the runners' cudaMallocHost packet staging. */
+int ffnrm_host_register(void *ptr, size_t bytes);
+int ffnrm_host_unregister(void *ptr);
+
+/* Convert f32 [n] -> fp16 [n] on `stream` (used after a cross-GPU allreduce of y_f32). */
+int ffnrm_cast_f16(const float *src, uint16_t *dst, int64_t n, void *stream);
+
+/* Device bytes held by loaded weights / workspace (for the bench's byte accounting). */
+int ffnrm_layer_bytes(ffnrm_ctx *ctx, int layer, int64_t *residual_bytes, int64_t *down_bytes);
+
+/* Kernel launches issued by this context since creation (the bench's launch count). */
+int64_t ffnrm_launch_count(ffnrm_ctx *ctx);
+
+/* Live per-kernel timing with CUDA events recorded on the launching stream around
+ * each of this context's kernel launches (off by default; enabling clears the
+ * totals). Kinds: FFNRM_KERNEL_RESIDUAL, FFNRM_KERNEL_DOWN, FFNRM_KERNEL_REDUCE.
+ * ffnrm_profile_read waits for the recorded events and returns the summed device
+ * time and the launch count of that kind since enabling. */
+#define FFNRM_KERNEL_RESIDUAL 0
+#define FFNRM_KERNEL_DOWN 1
+#define FFNRM_KERNEL_REDUCE 2
+int ffnrm_profile_enable(ffnrm_ctx *ctx, int enable);
+int ffnrm_profile_read(ffnrm_ctx *ctx, int kind, double *total_ms, int64_t *launches);
+
+const char *ffnrm_last_error(void);
+const char *ffnrm_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FFNRM_H */
