@@ -259,6 +259,16 @@ def run_ours(args, cfg, rank, world, local_rank):
     # unprofiled device timing (profiling events add host work between launches)
     dev_ms_plain, _, _ = timed(step_device, args.steps)
 
+    per_batch = {}
+    for T in cfg.tokens:
+        def one_batch(T=T):
+            for l in range(cfg.layers):
+                b = inputs[(T, l)]
+                stack.forward(l, b["z"], b["s"], b["gb"], b["ub"], b["y16"])
+        ms_b, _, prof_b = timed(one_batch, args.steps, profile=True)
+        per_batch[str(T)] = {"ms_per_stack": ms_b / args.steps, "tokens_per_s": T * args.steps / (ms_b / 1e3),
+                             "us_per_layer": {k: 1e3 * v[0] / max(v[1], 1) for k, v in prof_b.items() if v[1]}}
+
     tokens_step = sum(cfg.tokens)
     value = tokens_step * args.steps / (dev_ms_plain / 1e3)
     e2e_value = tokens_step * args.steps / (e2e_ms / 1e3)
@@ -315,7 +325,7 @@ def run_ours(args, cfg, rank, world, local_rank):
             "config": config_block(cfg, world),
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d * world,
                     "d2h_bytes_per_step": d2h * world, "ms_per_step": e2e_ms / args.steps},
-            "roofline": roofline, "residual_kernel": residual_kernel, "kernels": kern,
+            "roofline": roofline, "residual_kernel": residual_kernel, "kernels": kern, "per_batch": per_batch,
             "cpu_baseline": cpu, "gpu_launches": launches, "clocks": clock_info,
             "setup_s": round(setup_s, 1),
         }))

@@ -64,8 +64,8 @@ struct ffnrm_ctx {
     std::vector<LayerDev> layers;
     // workspace
     float *res[2] = {nullptr, nullptr};  // [Tm, F]
-    float *partial = nullptr;            // [max_splits, Tm, D]
-    int max_splits = 16;
+    float *partial = nullptr;            // [max_splits, 4, D] split-K partials of one token chunk
+    int max_splits = 64;
     // host-streamed mode staging
     int8_t *z_dev = nullptr;
     float *s_dev = nullptr;
@@ -123,30 +123,41 @@ int upload(DevBuf &b, const void *host, size_t bytes) {
     return FFNRM_OK;
 }
 
-// Row-pack codes [F, D] (values 0..3 after shifting) into the pair layout.
-void pack_pair(const uint8_t *q, int shift, int64_t F, int64_t D, std::vector<uint8_t> &out) {
-    out.assign(size_t(F * D / 4), 0);
+// Pack bits [shift, shift+1] of codes [F, D] into the interleaved pair layout
+// [F32][G/2][32][16 B] (see ffnrm_common.cuh). Padding rows are zero.
+void pack_pair_il(const uint8_t *q, int shift, int64_t F, int64_t D, std::vector<uint8_t> &out) {
+    const int64_t F32 = (F + 31) / 32, C = D / 64;
+    out.assign(size_t(F32 * C * 32 * 16), 0);
     for (int64_t r = 0; r < F; ++r) {
         const uint8_t *src = q + r * D;
-        uint8_t *dst = out.data() + r * (D / 4);
-        for (int64_t j = 0; j < D / 4; ++j) {
-            uint8_t v = 0;
-            for (int i = 0; i < 4; ++i) v |= uint8_t(((src[4 * j + i] >> shift) & 3) << (2 * i));
-            dst[j] = v;
+        for (int64_t c = 0; c < C; ++c) {
+            uint32_t *rec = reinterpret_cast<uint32_t *>(out.data() + (((r / 32) * C + c) * 32 + (r % 32)) * 16);
+            for (int j = 0; j < 4; ++j) {
+                const uint8_t *codes = src + 64 * c + 16 * j;  // group 2c + (j>>1), half j&1
+                uint32_t w = 0;
+                for (int i = 0; i < 4; ++i)
+                    for (int b = 0; b < 4; ++b) w |= uint32_t((codes[4 * i + b] >> shift) & 3) << (8 * b + 2 * i);
+                rec[j] = w;
+            }
         }
     }
 }
 
-// Row-pack bit `bit` of codes [F, D] into the plane layout.
-void pack_plane(const uint8_t *q, int bit, int64_t F, int64_t D, std::vector<uint8_t> &out) {
-    out.assign(size_t(F * D / 8), 0);
+// Pack bit `bit` of codes [F, D] into the interleaved plane layout [F32][G/2][32][8 B].
+void pack_plane_il(const uint8_t *q, int bit, int64_t F, int64_t D, std::vector<uint8_t> &out) {
+    const int64_t F32 = (F + 31) / 32, C = D / 64;
+    out.assign(size_t(F32 * C * 32 * 8), 0);
     for (int64_t r = 0; r < F; ++r) {
         const uint8_t *src = q + r * D;
-        uint8_t *dst = out.data() + r * (D / 8);
-        for (int64_t j = 0; j < D / 8; ++j) {
-            uint8_t v = 0;
-            for (int i = 0; i < 8; ++i) v |= uint8_t(((src[8 * j + i] >> bit) & 1) << i);
-            dst[j] = v;
+        for (int64_t c = 0; c < C; ++c) {
+            uint32_t *rec = reinterpret_cast<uint32_t *>(out.data() + (((r / 32) * C + c) * 32 + (r % 32)) * 8);
+            for (int j = 0; j < 2; ++j) {
+                const uint8_t *codes = src + 64 * c + 32 * j;
+                uint32_t w = 0;
+                for (int i = 0; i < 8; ++i)
+                    for (int b = 0; b < 4; ++b) w |= uint32_t((codes[4 * i + b] >> bit) & 1) << (8 * b + i);
+                rec[j] = w;
+            }
         }
     }
 }
@@ -206,12 +217,31 @@ bool all_half_exact(const float *v, int64_t n) {
     return true;
 }
 
-int upload_scales(DevBuf &b, const float *v, int64_t n, bool as_half) {
-    if (!as_half) return upload(b, v, size_t(n) * 4);
+// Per-group scales [F, G] -> interleaved [F32][G/2][32][2] (fp16 or f32).
+int upload_scales(DevBuf &b, const float *v, int64_t F, int64_t G, bool as_half) {
+    const int64_t F32 = (F + 31) / 32, C = G / 2, n = F32 * C * 32 * 2;
+    std::vector<float> il(size_t(n), 0.f);
+    for (int64_t r = 0; r < F; ++r)
+        for (int64_t c = 0; c < C; ++c)
+            for (int e = 0; e < 2; ++e)
+                il[size_t((((r / 32) * C + c) * 32 + (r % 32)) * 2 + e)] = v[r * G + 2 * c + e];
+    if (!as_half) return upload(b, il.data(), size_t(n) * 4);
     std::vector<__half> h{};
     h.resize(size_t(n));
-    for (int64_t i = 0; i < n; ++i) h[size_t(i)] = __float2half_rn(v[i]);
+    for (int64_t i = 0; i < n; ++i) h[size_t(i)] = __float2half_rn(il[size_t(i)]);
     return upload(b, h.data(), size_t(n) * 2);
+}
+
+// fp16 down [D, ld] (F used columns) -> interleaved [D/32][F/8][32][8].
+int upload_down(DevBuf &b, const uint16_t *down, int64_t ld, int64_t F, int64_t D) {
+    const int64_t Fc = F / 8;
+    std::vector<uint16_t> il(size_t(D * F));
+    for (int64_t o = 0; o < D; ++o) {
+        const uint16_t *row = down + o * ld;
+        for (int64_t c = 0; c < Fc; ++c)
+            std::memcpy(il.data() + (((o / 32) * Fc + c) * 32 + (o % 32)) * 8, row + 8 * c, 16);
+    }
+    return upload(b, il.data(), il.size() * 2);
 }
 
 void free_layer(LayerDev &L) {
@@ -232,6 +262,8 @@ int check_ctx(ffnrm_ctx *ctx, int layer) {
     if (!ctx->layers[size_t(layer)].loaded) return fail(FFNRM_ERR_STATE, "layer %d is not loaded", layer);
     return FFNRM_OK;
 }
+
+bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 int check_tokens(ffnrm_ctx *ctx, int tokens) {
     if (tokens < 1 || tokens > ctx->cfg.max_tokens)
@@ -273,16 +305,15 @@ struct ProfScope {
 // ---------------------------------------------------------------------------
 // Kernel launchers
 // ---------------------------------------------------------------------------
-template <int RB, int TT, int R, bool AH>
+template <int RB, int TT, bool AH>
 int launch_residual_t(ffnrm_ctx *ctx, ffnrm::ResidualParams &p, cudaStream_t st) {
-    const size_t smem = ffnrm::residual_smem_bytes(TT, p.G, p.need_pair, p.need_plane);
-    auto kern = ffnrm::residual_dp4a_kernel<RB, TT, R, AH>;
+    const size_t smem = ffnrm::residual_smem_bytes(TT, p.D);
+    auto kern = ffnrm::residual_gemv_kernel<RB, TT, AH>;
     if (smem > 48 * 1024) FFNRM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-    const int rows_per_cta = 8 * R;
-    p.row_blocks = (p.F + rows_per_cta - 1) / rows_per_cta;
+    p.row_blocks = (p.F + 31) / 32;
     dim3 grid(unsigned(2 * p.row_blocks), unsigned((p.T + TT - 1) / TT));
     ProfScope prof(ctx, st, FFNRM_KERNEL_RESIDUAL);
-    kern<<<grid, 256, smem, st>>>(p);
+    kern<<<grid, ffnrm::kResWarps * 32, smem, st>>>(p);
     ctx->launches++;
     FFNRM_CUDA(cudaGetLastError());
     return FFNRM_OK;
@@ -290,8 +321,7 @@ int launch_residual_t(ffnrm_ctx *ctx, ffnrm::ResidualParams &p, cudaStream_t st)
 
 template <int RB, int TT>
 int launch_residual_tt(ffnrm_ctx *ctx, ffnrm::ResidualParams &p, bool half, cudaStream_t st) {
-    constexpr int R = RB == 3 ? 2 : 4;
-    return half ? launch_residual_t<RB, TT, R, true>(ctx, p, st) : launch_residual_t<RB, TT, R, false>(ctx, p, st);
+    return half ? launch_residual_t<RB, TT, true>(ctx, p, st) : launch_residual_t<RB, TT, false>(ctx, p, st);
 }
 
 template <int RB>
@@ -308,8 +338,8 @@ int enqueue_residual(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s,
         return fail(FFNRM_ERR_STATE, "fallback tiles given but layer %d was loaded without fallback data", layer);
     ffnrm::ResidualParams p{};
     for (int q = 0; q < 2; ++q)
-        p.proj[q] = ffnrm::ProjView{static_cast<const uint8_t *>(L.pair[q].ptr), static_cast<const uint8_t *>(L.plane[q].ptr),
-                                    static_cast<const uint8_t *>(L.pair_hi[q].ptr), L.alpha[q].ptr, L.beta[q].ptr};
+        p.proj[q] = ffnrm::ProjView{static_cast<const uint4 *>(L.pair[q].ptr), static_cast<const uint2 *>(L.plane[q].ptr),
+                                    static_cast<const uint4 *>(L.pair_hi[q].ptr), L.alpha[q].ptr, L.beta[q].ptr};
     p.z = z;
     p.s = s;
     p.out[0] = gate_res;
@@ -322,8 +352,6 @@ int enqueue_residual(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s,
     p.T = T;
     p.tile_rows = ctx->cfg.base_tile_rows;
     const int r = ctx->cfg.residual_bits;
-    p.need_pair = (r != 1) || tiles != nullptr;
-    p.need_plane = r != 2;
     switch (r) {
         case 1: return launch_residual_rb<1>(ctx, p, L.scales_half, st);
         case 2: return launch_residual_rb<2>(ctx, p, L.scales_half, st);
@@ -341,14 +369,15 @@ int enqueue_down(ffnrm_ctx *ctx, int layer, int T, const float *gate_base, const
     p.gate_base = gate_base;
     p.up_base = up_base;
     p.fallback_tiles = tiles;
-    p.down = static_cast<const __half *>(L.down.ptr);
+    p.down_il = static_cast<const uint4 *>(L.down.ptr);
     p.partial = ctx->partial;
     p.F = F;
     p.D = D;
     p.T = T;
     p.tile_rows = ctx->cfg.base_tile_rows;
-    const int otiles = D / ffnrm::kDownTileRows;
-    int splits = std::max(1, std::min(ctx->max_splits, (2 * ctx->num_sms + otiles - 1) / otiles));
+    const int oblocks = D / ffnrm::kDownBlockRows;
+    // Enough split-K slices for ~4 CTAs per SM; slices are multiples of 8 rows of d_ff.
+    int splits = std::max(1, std::min(ctx->max_splits, (4 * ctx->num_sms + oblocks - 1) / oblocks));
     int kc = (F + splits - 1) / splits;
     kc = (kc + 7) / 8 * 8;
     splits = (F + kc - 1) / kc;
@@ -356,25 +385,32 @@ int enqueue_down(ffnrm_ctx *ctx, int layer, int T, const float *gate_base, const
     p.kc = kc;
     const int TT = T == 1 ? 1 : (T == 2 ? 2 : 4);
     const size_t smem = size_t(TT) * kc * sizeof(float);
-    dim3 grid(unsigned(otiles), unsigned(splits), unsigned((T + TT - 1) / TT));
-    auto run = [&](auto kern) -> int {
-        if (smem > 48 * 1024) FFNRM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-        ProfScope prof(ctx, st, FFNRM_KERNEL_DOWN);
-        kern<<<grid, 256, smem, st>>>(p);
+    for (int t0 = 0; t0 < T; t0 += TT) {
+        p.t0 = t0;
+        auto run = [&](auto kern) -> int {
+            if (smem > 48 * 1024)
+                FFNRM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+            ProfScope prof(ctx, st, FFNRM_KERNEL_DOWN);
+            kern<<<dim3(unsigned(oblocks), unsigned(splits)), ffnrm::kDownWarps * 32, smem, st>>>(p);
+            ctx->launches++;
+            FFNRM_CUDA(cudaGetLastError());
+            return FFNRM_OK;
+        };
+        int rc = TT == 1 ? run(ffnrm::down_gemv_kernel<1>)
+                         : (TT == 2 ? run(ffnrm::down_gemv_kernel<2>) : run(ffnrm::down_gemv_kernel<4>));
+        if (rc) return rc;
+        const int rows = std::min(TT, T - t0);
+        const int64_t n = int64_t(rows) * D;
+        const int blocks = int(std::min<int64_t>((n + 255) / 256, 4 * ctx->num_sms));
+        {
+            ProfScope prof(ctx, st, FFNRM_KERNEL_REDUCE);
+            ffnrm::splitk_reduce_kernel<<<blocks, 256, 0, st>>>(
+                ctx->partial, splits, TT, rows, D, y32 ? y32 + int64_t(t0) * D : nullptr,
+                y16 ? reinterpret_cast<__half *>(y16) + int64_t(t0) * D : nullptr);
+        }
         ctx->launches++;
         FFNRM_CUDA(cudaGetLastError());
-        return FFNRM_OK;
-    };
-    int rc = TT == 1 ? run(ffnrm::swiglu_down_kernel<1>) : (TT == 2 ? run(ffnrm::swiglu_down_kernel<2>) : run(ffnrm::swiglu_down_kernel<4>));
-    if (rc) return rc;
-    const int64_t n = int64_t(T) * D;
-    const int blocks = int(std::min<int64_t>((n + 255) / 256, 4 * ctx->num_sms));
-    {
-        ProfScope prof(ctx, st, FFNRM_KERNEL_REDUCE);
-        ffnrm::splitk_reduce_kernel<<<blocks, 256, 0, st>>>(ctx->partial, splits, n, y32, reinterpret_cast<__half *>(y16));
     }
-    ctx->launches++;
-    FFNRM_CUDA(cudaGetLastError());
     return FFNRM_OK;
 }
 
@@ -408,7 +444,7 @@ int ffnrm_create(ffnrm_ctx **out, int device, const ffnrm_config *cfg) {
     const size_t TF = size_t(c.max_tokens) * c.d_ff, TD = size_t(c.max_tokens) * c.d_model;
     const int ntiles = (c.d_ff + c.base_tile_rows - 1) / c.base_tile_rows;
     bool ok = cudaMalloc(&ctx->res[0], TF * 4) == cudaSuccess && cudaMalloc(&ctx->res[1], TF * 4) == cudaSuccess &&
-              cudaMalloc(&ctx->partial, size_t(ctx->max_splits) * TD * 4) == cudaSuccess &&
+              cudaMalloc(&ctx->partial, size_t(ctx->max_splits) * 4 * c.d_model * 4) == cudaSuccess &&
               cudaMalloc(&ctx->z_dev, TD) == cudaSuccess &&
               cudaMalloc(&ctx->s_dev, size_t(c.max_tokens) * ctx->G * 4) == cudaSuccess &&
               cudaMalloc(&ctx->y16_dev, TD * 2) == cudaSuccess;
@@ -482,28 +518,21 @@ int ffnrm_load_layer(ffnrm_ctx *ctx, int layer, const ffnrm_layer_weights *w) {
         if (rc) break;
         if (r != 1 || L.has_fallback) {
             // bits 0-1 of the full code equal the low two residual bits for r >= 2
-            pack_pair(have_full ? full.data() : lo.data(), 0, F, D, packed);
+            pack_pair_il(have_full ? full.data() : lo.data(), 0, F, D, packed);
             if ((rc = upload(L.pair[q], packed.data(), packed.size()))) break;
         }
         if (r != 2) {
-            pack_plane(lo.data(), r == 1 ? 0 : 2, F, D, packed);
+            pack_plane_il(lo.data(), r == 1 ? 0 : 2, F, D, packed);
             if ((rc = upload(L.plane[q], packed.data(), packed.size()))) break;
         }
         if (L.has_fallback) {
-            pack_pair(full.data(), 2, F, D, packed);
+            pack_pair_il(full.data(), 2, F, D, packed);
             if ((rc = upload(L.pair_hi[q], packed.data(), packed.size()))) break;
-            if ((rc = upload_scales(L.beta[q], beta[q], F * G, L.scales_half))) break;
+            if ((rc = upload_scales(L.beta[q], beta[q], F, G, L.scales_half))) break;
         }
-        rc = upload_scales(L.alpha[q], alpha[q], F * G, L.scales_half);
+        rc = upload_scales(L.alpha[q], alpha[q], F, G, L.scales_half);
     }
-    if (rc == FFNRM_OK) {
-        rc = dev_alloc(L.down, size_t(D * F * 2));
-        if (rc == FFNRM_OK) {
-            cudaError_t e = cudaMemcpy2D(L.down.ptr, size_t(F) * 2, w->down, size_t(w->down_ld) * 2, size_t(F) * 2,
-                                         size_t(D), cudaMemcpyHostToDevice);
-            if (e != cudaSuccess) rc = fail(FFNRM_ERR_CUDA, "down upload failed: %s", cudaGetErrorString(e));
-        }
-    }
+    if (rc == FFNRM_OK) rc = upload_down(L.down, w->down, w->down_ld, F, D);
     if (rc) {
         free_layer(L);
         return rc;
@@ -518,6 +547,8 @@ int ffnrm_residual(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s, i
     if (rc) return rc;
     if ((rc = check_tokens(ctx, tokens))) return rc;
     if (!z || !s || !gate_res || !up_res) return fail(FFNRM_ERR_ARG, "null device pointer");
+    if (!aligned(z, 16) || !aligned(s, 4) || !aligned(gate_res, 4) || !aligned(up_res, 4) || !aligned(group_dots, 8))
+        return fail(FFNRM_ERR_ARG, "z must be 16-byte aligned and s/outputs 4-byte aligned (dots 8-byte)");
     DeviceGuard guard(ctx->device);
     return enqueue_residual(ctx, layer, z, s, tokens, gate_res, up_res, group_dots, fallback_tiles,
                             static_cast<cudaStream_t>(stream));
@@ -531,6 +562,9 @@ int ffnrm_ffn_forward(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s
     if ((rc = check_tokens(ctx, tokens))) return rc;
     if (!z || !s || !gate_base || !up_base) return fail(FFNRM_ERR_ARG, "null device pointer");
     if (!y_f32 && !y_f16) return fail(FFNRM_ERR_ARG, "no output requested");
+    if (!aligned(z, 16) || !aligned(s, 4) || !aligned(gate_base, 4) || !aligned(up_base, 4) || !aligned(y_f32, 4) ||
+        !aligned(y_f16, 2))
+        return fail(FFNRM_ERR_ARG, "z must be 16-byte aligned and s, base sums and outputs element-aligned");
     DeviceGuard guard(ctx->device);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if ((rc = enqueue_residual(ctx, layer, z, s, tokens, ctx->res[0], ctx->res[1], nullptr, fallback_tiles, st))) return rc;

@@ -1,25 +1,24 @@
 // Shared device-side definitions for the B200 exact base/residual split kernels.
 //
-// Device layout of one projection (gate or up) of one layer, rows = d_ff rows held
-// by this context, D = d_model, G = D/32:
-//   pair    : bits 0-1 of every code, row-packed [F, D/4]; byte j of a row holds codes
-//             4j..4j+3 at bit pairs 0,2,4,6 (the reference QLO2 layout,
-//             scripts/export_cuda_residual_artifact_v2.py:13-24). Present for r in
-//             {2,3} and whenever fallback data is kept.
-//   plane   : one bit of every code, row-packed [F, D/8], code 8j+i at bit i of byte j
-//             (one plane of scripts/compile_q4k_host_base_gpu_residual.py:17-26):
-//             bit 0 for r = 1, bit 2 for r = 3.
-//   pair_hi : bits 2-3 of every code in the pair layout (fallback tiles only).
-//   alpha   : [F, G] fp16 when lossless, else f32; beta likewise (fallback only).
+// Device layouts (chosen at load time; the host converts from the reference's
+// artifact formats). F32 = ceil(F/32) row blocks, C = G/2 chunks of two 32-code
+// groups, "il" = 32 rows interleaved so that lane l of a warp owns row 32*rb + l and
+// one warp-wide load of chunk c reads 32 consecutive 16-byte (or 8-byte) records:
 //
-// The residual group dot of row f, group g, token t is
-//   r = 1: P = dot(plane, z)      r = 2: P = dot(pair, z)     r = 3: P = dot(pair, z) + 4*dot(plane, z)
-// and the unsplit fallback dot is  dot(pair, z) + 4*dot(pair_hi, z).
+//   pair_il  [F32][C][32][16 B]  bits 0-1 of every code. Word j of a record holds group
+//            2c + (j>>1), codes 16*(j&1) .. +15; code 4i+b of those 16 sits at bit 8b+2i,
+//            so (w >> 2i) & 0x03030303 is the dp4a operand for activations 4i..4i+3 in
+//            natural order.
+//   plane_il [F32][C][32][8 B]   one bit of every code (bit 0 for r = 1, bit 2 for r = 3).
+//            Word j holds group 2c + j; code 4i+b at bit 8b+i, so (w >> i) & 0x01010101
+//            pairs with activations 4i..4i+3.
+//   pair_hi  like pair_il, bits 2-3 (fallback tiles only).
+//   alpha/beta [F32][C][32][2]   fp16 when lossless, else f32.
+//   down_il  [D/32][F/8][32][8 fp16]  the down weight, output row o = 32*ob + lane.
 //
-// dp4a operand order. A 32-bit word of `pair` holds 16 codes; (w >> 2i) & 0x03030303
-// yields codes {16m+i, 16m+4+i, 16m+8+i, 16m+12+i} (m = word index), so activations
-// are stored permuted in shared memory to match (zpair). A 32-bit word of `plane`
-// holds one group; (w >> i) & 0x01010101 yields codes {i, 8+i, 16+i, 24+i} (zplane).
+// Rows F..32*F32-1 are zero padding. The residual group dot of row f, group g is
+//   r = 1: P = dot(plane, z)   r = 2: P = dot(pair, z)   r = 3: P = dot(pair, z) + 4 dot(plane, z)
+// and the unsplit fallback dot is dot(pair, z) + 4 dot(pair_hi, z).
 #pragma once
 
 #include <cuda_fp16.h>
@@ -31,35 +30,58 @@ namespace ffnrm {
 constexpr int kGroup = 32;
 
 struct ProjView {
-    const uint8_t *pair;
-    const uint8_t *plane;
-    const uint8_t *pair_hi;
+    const uint4 *pair;
+    const uint2 *plane;
+    const uint4 *pair_hi;
     const void *alpha;
     const void *beta;
 };
 
 template <bool HALF>
-__device__ __forceinline__ void load_scale2(const void *base, int64_t index, float &a0, float &a1) {
+__device__ __forceinline__ void load_scale2(const void *base, int64_t record, float &a0, float &a1) {
     if constexpr (HALF) {
-        const __half2 v = *reinterpret_cast<const __half2 *>(reinterpret_cast<const __half *>(base) + index);
+        const __half2 v = __ldg(reinterpret_cast<const __half2 *>(base) + record);
         const float2 f = __half22float2(v);
         a0 = f.x;
         a1 = f.y;
     } else {
-        const float2 v = *reinterpret_cast<const float2 *>(reinterpret_cast<const float *>(base) + index);
+        const float2 v = __ldg(reinterpret_cast<const float2 *>(base) + record);
         a0 = v.x;
         a1 = v.y;
     }
 }
 
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-
 __device__ __forceinline__ bool row_flagged(const uint8_t *tiles, int row, int tile_rows) {
     return tiles != nullptr && tiles[row / tile_rows] != 0;
+}
+
+// Exact dot of one 32-code group in the pair layout (words lo = codes 0-15,
+// hi = codes 16-31) with 8 natural-order activation words.
+__device__ __forceinline__ int dot_pair(uint32_t lo, uint32_t hi, const uint4 &z0, const uint4 &z1) {
+    constexpr uint32_t M = 0x03030303u;
+    int a = __dp4a(int(lo & M), int(z0.x), 0);
+    a = __dp4a(int((lo >> 2) & M), int(z0.y), a);
+    a = __dp4a(int((lo >> 4) & M), int(z0.z), a);
+    a = __dp4a(int((lo >> 6) & M), int(z0.w), a);
+    a = __dp4a(int(hi & M), int(z1.x), a);
+    a = __dp4a(int((hi >> 2) & M), int(z1.y), a);
+    a = __dp4a(int((hi >> 4) & M), int(z1.z), a);
+    a = __dp4a(int((hi >> 6) & M), int(z1.w), a);
+    return a;
+}
+
+// Exact dot of one 32-code group in the plane layout with 8 activation words.
+__device__ __forceinline__ int dot_plane(uint32_t w, const uint4 &z0, const uint4 &z1) {
+    constexpr uint32_t M = 0x01010101u;
+    int a = __dp4a(int(w & M), int(z0.x), 0);
+    a = __dp4a(int((w >> 1) & M), int(z0.y), a);
+    a = __dp4a(int((w >> 2) & M), int(z0.z), a);
+    a = __dp4a(int((w >> 3) & M), int(z0.w), a);
+    a = __dp4a(int((w >> 4) & M), int(z1.x), a);
+    a = __dp4a(int((w >> 5) & M), int(z1.y), a);
+    a = __dp4a(int((w >> 6) & M), int(z1.z), a);
+    a = __dp4a(int((w >> 7) & M), int(z1.w), a);
+    return a;
 }
 
 }  // namespace ffnrm

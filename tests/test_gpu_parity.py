@@ -31,7 +31,9 @@ def rel_l2(a, b):
 def close_rows(actual, expected, rtol=1e-5):
     """fp32 accumulation vs float64: error bounded relative to the row's magnitude scale."""
     scale = np.maximum(np.abs(expected).max(axis=-1, keepdims=True), 1e-30)
-    np.testing.assert_array_less(np.abs(np.asarray(actual, np.float64) - expected), rtol * scale + 1e-30)
+    err = np.abs(np.asarray(actual, np.float64) - expected)
+    bound = np.broadcast_to(rtol * scale, err.shape)
+    assert (err <= bound).all(), f"max err/scale {float((err / scale).max()):.3e} > {rtol}"
 
 
 def make_ctx(c, tokens=None, keep_fallback=True):
