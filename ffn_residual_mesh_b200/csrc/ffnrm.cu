@@ -17,9 +17,10 @@
 #include <string>
 #include <vector>
 
-#include "down_gemv.cuh"
+#include "down_mma.cuh"
 #include "ffnrm_common.cuh"
 #include "residual_dp4a.cuh"
+#include "residual_mma.cuh"
 
 namespace {
 
@@ -64,7 +65,8 @@ struct ffnrm_ctx {
     std::vector<LayerDev> layers;
     // workspace
     float *res[2] = {nullptr, nullptr};  // [Tm, F]
-    float *partial = nullptr;            // [max_splits, 4, D] split-K partials of one token chunk
+    float *partial = nullptr;            // [max_splits, 64, D] split-K partials of one token chunk
+    int *tickets = nullptr;              // [D/256] split-K arrival counters (self-resetting)
     int max_splits = 64;
     // host-streamed mode staging
     int8_t *z_dev = nullptr;
@@ -232,16 +234,24 @@ int upload_scales(DevBuf &b, const float *v, int64_t F, int64_t G, bool as_half)
     return upload(b, h.data(), size_t(n) * 2);
 }
 
-// fp16 down [D, ld] (F used columns) -> interleaved [D/32][F/8][32][8].
+// fp16 down [D, ld] (F used columns) -> fragment-native [D/16][F16/16][32 lanes][4 words]:
+// lane 4g+t holds (row g, k 2t..2t+1), (row g+8, k 2t..), (row g, k 2t+8..), (row g+8, k 2t+8..)
+// of each 16x16 tile, the m16n8k16 A registers. Columns F..F16-1 are zero.
 int upload_down(DevBuf &b, const uint16_t *down, int64_t ld, int64_t F, int64_t D) {
-    const int64_t Fc = F / 8;
-    std::vector<uint16_t> il(size_t(D * F));
-    for (int64_t o = 0; o < D; ++o) {
-        const uint16_t *row = down + o * ld;
-        for (int64_t c = 0; c < Fc; ++c)
-            std::memcpy(il.data() + (((o / 32) * Fc + c) * 32 + (o % 32)) * 8, row + 8 * c, 16);
-    }
-    return upload(b, il.data(), il.size() * 2);
+    const int64_t F16 = (F + 15) / 16 * 16, KS = F16 / 16;
+    std::vector<uint16_t> fr(size_t(D * F16), 0);
+    auto at = [&](int64_t o, int64_t k) -> uint16_t { return k < F ? down[o * ld + k] : uint16_t(0); };
+    for (int64_t mt = 0; mt < D / 16; ++mt)
+        for (int64_t ks = 0; ks < KS; ++ks)
+            for (int lane = 0; lane < 32; ++lane) {
+                const int64_t g = lane / 4, t = lane % 4, r = mt * 16 + g, k = ks * 16 + 2 * t;
+                uint16_t *w = fr.data() + ((mt * KS + ks) * 32 + lane) * 8;
+                w[0] = at(r, k), w[1] = at(r, k + 1);
+                w[2] = at(r + 8, k), w[3] = at(r + 8, k + 1);
+                w[4] = at(r, k + 8), w[5] = at(r, k + 9);
+                w[6] = at(r + 8, k + 8), w[7] = at(r + 8, k + 9);
+            }
+    return upload(b, fr.data(), fr.size() * 2);
 }
 
 void free_layer(LayerDev &L) {
@@ -266,8 +276,8 @@ int check_ctx(ffnrm_ctx *ctx, int layer) {
 bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 int check_tokens(ffnrm_ctx *ctx, int tokens) {
-    if (tokens < 1 || tokens > ctx->cfg.max_tokens)
-        return fail(FFNRM_ERR_ARG, "tokens=%d outside [1, max_tokens=%d]", tokens, ctx->cfg.max_tokens);
+    if (tokens < 0 || tokens > ctx->cfg.max_tokens)
+        return fail(FFNRM_ERR_ARG, "tokens=%d outside [0, max_tokens=%d]", tokens, ctx->cfg.max_tokens);
     return FFNRM_OK;
 }
 
@@ -324,11 +334,39 @@ int launch_residual_tt(ffnrm_ctx *ctx, ffnrm::ResidualParams &p, bool half, cuda
     return half ? launch_residual_t<RB, TT, true>(ctx, p, st) : launch_residual_t<RB, TT, false>(ctx, p, st);
 }
 
+template <int RB, int NT, bool AH, bool FB>
+int launch_residual_mma_t(ffnrm_ctx *ctx, ffnrm::ResidualParams &p, cudaStream_t st) {
+    constexpr int TN = NT * 8;
+    const size_t smem = ffnrm::residual_mma_smem_bytes(TN, p.G, FB);
+    auto kern = ffnrm::residual_mma_kernel<RB, NT, AH, FB>;
+    if (smem > 48 * 1024) FFNRM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+    constexpr int warps = 4;
+    p.row_blocks = (p.F + 31) / 32;
+    const int per_proj = (p.row_blocks + warps - 1) / warps;
+    dim3 grid(unsigned(2 * per_proj), unsigned((p.T + TN - 1) / TN));
+    ProfScope prof(ctx, st, FFNRM_KERNEL_RESIDUAL);
+    kern<<<grid, warps * 32, smem, st>>>(p);
+    ctx->launches++;
+    FFNRM_CUDA(cudaGetLastError());
+    return FFNRM_OK;
+}
+
+template <int RB, int NT>
+int launch_residual_mma_nt(ffnrm_ctx *ctx, ffnrm::ResidualParams &p, bool half, cudaStream_t st) {
+    const bool fb = p.fallback_tiles != nullptr;
+    if (half) return fb ? launch_residual_mma_t<RB, NT, true, true>(ctx, p, st) : launch_residual_mma_t<RB, NT, true, false>(ctx, p, st);
+    return fb ? launch_residual_mma_t<RB, NT, false, true>(ctx, p, st) : launch_residual_mma_t<RB, NT, false, false>(ctx, p, st);
+}
+
+// T <= 4: dp4a GEMV (HBM-bound); larger batches: int8 tensor-core MMA tiles.
 template <int RB>
 int launch_residual_rb(ffnrm_ctx *ctx, ffnrm::ResidualParams &p, bool half, cudaStream_t st) {
     if (p.T == 1) return launch_residual_tt<RB, 1>(ctx, p, half, st);
     if (p.T == 2) return launch_residual_tt<RB, 2>(ctx, p, half, st);
-    return launch_residual_tt<RB, 4>(ctx, p, half, st);
+    if (p.T <= 4) return launch_residual_tt<RB, 4>(ctx, p, half, st);
+    if (p.T <= 8) return launch_residual_mma_nt<RB, 1>(ctx, p, half, st);
+    if (p.T <= 16) return launch_residual_mma_nt<RB, 2>(ctx, p, half, st);
+    return launch_residual_mma_nt<RB, 4>(ctx, p, half, st);  // 32-token tiles (64 would spill)
 }
 
 int enqueue_residual(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s, int T, float *gate_res,
@@ -359,57 +397,55 @@ int enqueue_residual(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s,
     }
 }
 
+template <int NT>
+int launch_down_t(ffnrm_ctx *ctx, ffnrm::DownMmaParams &p, dim3 grid, cudaStream_t st) {
+    const size_t smem = ffnrm::down_mma_smem_bytes(NT * 8);
+    auto kern = ffnrm::down_mma_kernel<NT>;
+    if (smem > 48 * 1024) FFNRM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+    ProfScope prof(ctx, st, FFNRM_KERNEL_DOWN);
+    kern<<<grid, ffnrm::kDownWarpsMma * 32, smem, st>>>(p);
+    ctx->launches++;
+    FFNRM_CUDA(cudaGetLastError());
+    return FFNRM_OK;
+}
+
 int enqueue_down(ffnrm_ctx *ctx, int layer, int T, const float *gate_base, const float *up_base,
                  const uint8_t *tiles, float *y32, uint16_t *y16, cudaStream_t st) {
     LayerDev &L = ctx->layers[size_t(layer)];
     const int F = ctx->cfg.d_ff, D = ctx->cfg.d_model;
-    ffnrm::DownParams p{};
+    const int F16 = (F + 15) / 16 * 16;
+    ffnrm::DownMmaParams p{};
     p.gate_res = ctx->res[0];
     p.up_res = ctx->res[1];
     p.gate_base = gate_base;
     p.up_base = up_base;
     p.fallback_tiles = tiles;
-    p.down_il = static_cast<const uint4 *>(L.down.ptr);
+    p.down_frag = static_cast<const uint4 *>(L.down.ptr);
     p.partial = ctx->partial;
+    p.tickets = ctx->tickets;
+    p.y32 = y32;
+    p.y16 = reinterpret_cast<__half *>(y16);
     p.F = F;
+    p.F16 = F16;
     p.D = D;
     p.T = T;
     p.tile_rows = ctx->cfg.base_tile_rows;
-    const int oblocks = D / ffnrm::kDownBlockRows;
-    // Enough split-K slices for ~4 CTAs per SM; slices are multiples of 8 rows of d_ff.
-    int splits = std::max(1, std::min(ctx->max_splits, (4 * ctx->num_sms + oblocks - 1) / oblocks));
-    int kc = (F + splits - 1) / splits;
-    kc = (kc + 7) / 8 * 8;
-    splits = (F + kc - 1) / kc;
+    const int oblocks = D / ffnrm::kDownRowsCta;
+    // ~2 CTAs per SM; slices are multiples of 16 rows of d_ff.
+    int splits = std::max(1, std::min(ctx->max_splits, (2 * ctx->num_sms + oblocks - 1) / oblocks));
+    int kc = (F16 + splits - 1) / splits;
+    kc = (kc + 15) / 16 * 16;
+    splits = (F16 + kc - 1) / kc;
     p.splits = splits;
     p.kc = kc;
-    const int TT = T == 1 ? 1 : (T == 2 ? 2 : 4);
-    const size_t smem = size_t(TT) * kc * sizeof(float);
-    for (int t0 = 0; t0 < T; t0 += TT) {
+    const int NT = T <= 8 ? 1 : (T <= 16 ? 2 : (T <= 32 ? 4 : 8));
+    const dim3 grid{unsigned(oblocks), unsigned(splits), 1u};
+    for (int t0 = 0; t0 < T; t0 += NT * 8) {
         p.t0 = t0;
-        auto run = [&](auto kern) -> int {
-            if (smem > 48 * 1024)
-                FFNRM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-            ProfScope prof(ctx, st, FFNRM_KERNEL_DOWN);
-            kern<<<dim3(unsigned(oblocks), unsigned(splits)), ffnrm::kDownWarps * 32, smem, st>>>(p);
-            ctx->launches++;
-            FFNRM_CUDA(cudaGetLastError());
-            return FFNRM_OK;
-        };
-        int rc = TT == 1 ? run(ffnrm::down_gemv_kernel<1>)
-                         : (TT == 2 ? run(ffnrm::down_gemv_kernel<2>) : run(ffnrm::down_gemv_kernel<4>));
+        int rc = NT == 1 ? launch_down_t<1>(ctx, p, grid, st)
+                         : NT == 2 ? launch_down_t<2>(ctx, p, grid, st)
+                                   : NT == 4 ? launch_down_t<4>(ctx, p, grid, st) : launch_down_t<8>(ctx, p, grid, st);
         if (rc) return rc;
-        const int rows = std::min(TT, T - t0);
-        const int64_t n = int64_t(rows) * D;
-        const int blocks = int(std::min<int64_t>((n + 255) / 256, 4 * ctx->num_sms));
-        {
-            ProfScope prof(ctx, st, FFNRM_KERNEL_REDUCE);
-            ffnrm::splitk_reduce_kernel<<<blocks, 256, 0, st>>>(
-                ctx->partial, splits, TT, rows, D, y32 ? y32 + int64_t(t0) * D : nullptr,
-                y16 ? reinterpret_cast<__half *>(y16) + int64_t(t0) * D : nullptr);
-        }
-        ctx->launches++;
-        FFNRM_CUDA(cudaGetLastError());
     }
     return FFNRM_OK;
 }
@@ -426,7 +462,7 @@ int ffnrm_create(ffnrm_ctx **out, int device, const ffnrm_config *cfg) {
     *out = nullptr;
     const ffnrm_config c = *cfg;
     if (c.d_model <= 0 || c.d_model % 256) return fail(FFNRM_ERR_ARG, "d_model=%d must be a positive multiple of 256", c.d_model);
-    if (c.d_ff <= 0 || c.d_ff % 8) return fail(FFNRM_ERR_ARG, "d_ff=%d must be a positive multiple of 8", c.d_ff);
+    if (c.d_ff <= 0) return fail(FFNRM_ERR_ARG, "d_ff=%d must be positive", c.d_ff);
     if (c.residual_bits < 1 || c.residual_bits > 3) return fail(FFNRM_ERR_ARG, "residual_bits=%d must be 1, 2 or 3", c.residual_bits);
     if (c.n_layers <= 0 || c.max_tokens <= 0) return fail(FFNRM_ERR_ARG, "n_layers and max_tokens must be positive");
     if (c.base_tile_rows <= 0) return fail(FFNRM_ERR_ARG, "base_tile_rows must be positive");
@@ -444,7 +480,9 @@ int ffnrm_create(ffnrm_ctx **out, int device, const ffnrm_config *cfg) {
     const size_t TF = size_t(c.max_tokens) * c.d_ff, TD = size_t(c.max_tokens) * c.d_model;
     const int ntiles = (c.d_ff + c.base_tile_rows - 1) / c.base_tile_rows;
     bool ok = cudaMalloc(&ctx->res[0], TF * 4) == cudaSuccess && cudaMalloc(&ctx->res[1], TF * 4) == cudaSuccess &&
-              cudaMalloc(&ctx->partial, size_t(ctx->max_splits) * 4 * c.d_model * 4) == cudaSuccess &&
+              cudaMalloc(&ctx->partial, size_t(ctx->max_splits) * 64 * c.d_model * 4) == cudaSuccess &&
+              cudaMalloc(&ctx->tickets, size_t(c.d_model / 256) * sizeof(int)) == cudaSuccess &&
+              cudaMemset(ctx->tickets, 0, size_t(c.d_model / 256) * sizeof(int)) == cudaSuccess &&
               cudaMalloc(&ctx->z_dev, TD) == cudaSuccess &&
               cudaMalloc(&ctx->s_dev, size_t(c.max_tokens) * ctx->G * 4) == cudaSuccess &&
               cudaMalloc(&ctx->y16_dev, TD * 2) == cudaSuccess;
@@ -473,6 +511,7 @@ int ffnrm_destroy(ffnrm_ctx *ctx) {
     cudaFree(ctx->res[0]);
     cudaFree(ctx->res[1]);
     cudaFree(ctx->partial);
+    cudaFree(ctx->tickets);
     cudaFree(ctx->z_dev);
     cudaFree(ctx->s_dev);
     cudaFree(ctx->y16_dev);
@@ -546,6 +585,7 @@ int ffnrm_residual(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s, i
     int rc = check_ctx(ctx, layer);
     if (rc) return rc;
     if ((rc = check_tokens(ctx, tokens))) return rc;
+    if (tokens == 0) return FFNRM_OK;  // empty batch
     if (!z || !s || !gate_res || !up_res) return fail(FFNRM_ERR_ARG, "null device pointer");
     if (!aligned(z, 16) || !aligned(s, 4) || !aligned(gate_res, 4) || !aligned(up_res, 4) || !aligned(group_dots, 8))
         return fail(FFNRM_ERR_ARG, "z must be 16-byte aligned and s/outputs 4-byte aligned (dots 8-byte)");
@@ -560,6 +600,7 @@ int ffnrm_ffn_forward(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s
     int rc = check_ctx(ctx, layer);
     if (rc) return rc;
     if ((rc = check_tokens(ctx, tokens))) return rc;
+    if (tokens == 0) return FFNRM_OK;  // empty batch
     if (!z || !s || !gate_base || !up_base) return fail(FFNRM_ERR_ARG, "null device pointer");
     if (!y_f32 && !y_f16) return fail(FFNRM_ERR_ARG, "no output requested");
     if (!aligned(z, 16) || !aligned(s, 4) || !aligned(gate_base, 4) || !aligned(up_base, 4) || !aligned(y_f32, 4) ||
@@ -577,6 +618,7 @@ int ffnrm_ffn_forward_host(ffnrm_ctx *ctx, int layer, const int8_t *z, const flo
     int rc = check_ctx(ctx, layer);
     if (rc) return rc;
     if ((rc = check_tokens(ctx, tokens))) return rc;
+    if (tokens == 0) return FFNRM_OK;  // empty batch
     if (!z || !s || !gate_base || !up_base || !y_f16) return fail(FFNRM_ERR_ARG, "null host pointer");
     DeviceGuard guard(ctx->device);
     cudaStream_t st = static_cast<cudaStream_t>(stream);

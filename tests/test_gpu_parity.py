@@ -236,3 +236,52 @@ def test_full_layer_shape_property(cuda):
                         gate_base=gb, up_base=ub)
     assert rel_l2(y32.cpu().numpy(), ref["y"]) < 1e-5
     ctx.close()
+
+
+@pytest.mark.parametrize("T,F,r", [(70, 1000, 2), (40, 333, 1), (33, 200, 3)])
+def test_multi_chunk_batches_ragged_rows(T, F, r, cuda):
+    """Batches spanning several token tiles of both tensor-core kernels, with a
+    d_ff that is not a multiple of the 32-row blocks."""
+    import torch
+    from ffn_residual_mesh_b200 import synth
+    from ffn_residual_mesh_b200.engine import LayerSpec, ResidualMesh
+    D = 1024
+    L = synth.make_layer(21 + r, F, D)
+    _, z, s = synth.make_activations(22 + T, T, D)
+    ctx = ResidualMesh(D, F, r, 1, T, base_tile_rows=64)
+    ctx.load_layer(0, LayerSpec(L.gate_codes, L.up_codes, L.gate_alpha, L.up_alpha, L.down, L.gate_beta, L.up_beta,
+                                keep_fallback=True))
+    g = torch.empty(T, F, device=cuda)
+    u = torch.empty_like(g)
+    dots = torch.empty((2, T, F, D // 32), dtype=torch.int32, device=cuda)
+    ctx.residual(0, dev(z, cuda), dev(s, cuda), g, u, dots)
+    gb = O.host_base(L.gate_codes, L.gate_alpha, L.gate_beta, z, s, r)
+    ub = O.host_base(L.up_codes, L.up_alpha, L.up_beta, z, s, r)
+    tiles = np.zeros(-(-F // 64), np.uint8)
+    tiles[1] = 1
+    y32 = torch.empty(T, D, device=cuda)
+    ctx.forward(0, dev(z, cuda), dev(s, cuda), dev(gb.astype(np.float32), cuda), dev(ub.astype(np.float32), cuda),
+                fallback_tiles=dev(tiles, cuda), y32=y32)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(dots.cpu().numpy()[0], O.group_dots(L.gate_codes & ((1 << r) - 1), z))
+    np.testing.assert_array_equal(dots.cpu().numpy()[1], O.group_dots(L.up_codes & ((1 << r) - 1), z))
+    close_rows(g.cpu().numpy(), O.residual(L.gate_codes, L.gate_alpha, z, s, r), rtol=2e-5)
+    ref = O.ffn_forward(L.gate_codes, L.up_codes, L.gate_alpha, L.up_alpha, L.gate_beta, L.up_beta, L.down, z, s, r,
+                        gate_base=gb, up_base=ub, fallback_tiles=tiles, tile_rows=64)
+    assert rel_l2(y32.cpu().numpy(), ref["y"]) < 1e-5
+    assert np.abs(y32.cpu().numpy() - ref["y"]).max() < Y_MAX_ABS
+    ctx.close()
+
+
+def test_empty_batch_is_a_no_op(cuda):
+    import torch
+    c = load("c1_decode_t1_r2")
+    F, D = int(c["F"]), int(c["D"])
+    ctx = make_ctx(c)
+    z = torch.empty(0, D, dtype=torch.int8, device=cuda)
+    s = torch.empty(0, D // 32, device=cuda)
+    e = torch.empty(0, F, device=cuda)
+    ctx.residual(0, z, s, e, e)
+    ctx.forward(0, z, s, e, e, y32=torch.empty(0, D, device=cuda))
+    torch.cuda.synchronize()
+    ctx.close()
