@@ -1,40 +1,38 @@
-// Merge + SwiGLU + fp16 down projection on tensor cores (mma.sync m16n8k16, f32 accumulate).
+// fp16 down projection on tensor cores (mma.sync m16n8k16, f32 accumulate).
 //
 // Replaces swiglu_down_kernel (src/exact_cpu_base_gpu_full_ffn_runner.cu:217-240) and
-// the torch.mm down of scripts/benchmark_gpu_full_ffn_density.py:162.
+// the torch.mm down of scripts/benchmark_gpu_full_ffn_density.py:162. The merge and
+// SwiGLU already happened in the residual kernel, which wrote h = SiLU(g)*u as two
+// fp16 parts (h = hi + lo to ~2^-22 relative), so y keeps fp32-level accuracy.
 //
-// Layout: the fp16 down weight is stored fragment-native, [D/16][F16/16][32 lanes][4 words]:
-// the 16 bytes a lane loads are exactly its A registers a0..a3 for one 16x16 tile, so a
-// warp streams 512 contiguous bytes per tile with one 128-bit load per lane.
-// Grid = (D/256 output blocks, split-K slices of d_ff). A CTA walks its d_ff slice in
-// chunks: it merges g = g_base + g_res and u = u_base + u_res, applies
-// h = g/(1+exp(-g))*u and splits h into fp16 hi + lo parts (h = hi + lo to ~2^-22
-// relative) in shared memory; each warp then runs two MMAs per tile (hi and lo) for its
-// 32 output rows against all tokens. Rows of flagged fallback tiles take the unsplit
-// projection that the residual kernel wrote into g_res/u_res (no base added).
-// Split-K partials go to a workspace; the last CTA of each output block (atomic
-// ticket) sums them in slice order, so results are deterministic, and writes y.
+// Layout: the fp16 down weight is fragment-native, [D/16][F16/16][32 lanes][4 words]:
+// the 16 bytes a lane loads are its A registers a0..a3 for one 16x16 tile, so a warp
+// streams 512 contiguous bytes per tile with one 128-bit load per lane.
+// Grid = (D/256 output blocks, split-K slices of d_ff). Each warp owns 32 output rows
+// (two M tiles) and all TN tokens; h of the CTA's slice is staged into shared memory by
+// cp.async one K chunk ahead. Split-K partials go to a workspace; the last CTA of each
+// output block (atomic ticket) sums them in slice order, so the result is
+// deterministic, and writes y in f32 and/or fp16.
 #pragma once
 
 #include "ffnrm_common.cuh"
+#include "residual_mma.cuh"
 
 namespace ffnrm {
 
 struct DownMmaParams {
-    const float *gate_res, *up_res;    // [T, F]
-    const float *gate_base, *up_base;  // [T, F]
-    const uint8_t *fallback_tiles;
-    const uint4 *down_frag;            // [D/16][F16/16][32] records
-    float *partial;                    // [splits][Tn][D] with Tn = NT*8
-    int *tickets;                      // [D/256] zero-initialised, self-resetting
-    float *y32;                        // [T, D] or null
-    __half *y16;                       // [T, D] or null
-    int F, F16, D, T, t0, tile_rows, splits, kc;
+    const __half *h_hi, *h_lo;  // [T, F16]
+    const uint4 *down_frag;     // [D/16][F16/16][32] records
+    float *partial;             // [splits][TN][D]
+    int *tickets;               // [D/256] zero-initialised, self-resetting
+    float *y32;                 // [T, D] or null
+    __half *y16;                // [T, D] or null
+    int F16, D, T, t0, splits, kc;
 };
 
 constexpr int kDownWarpsMma = 8;
 constexpr int kDownRowsCta = kDownWarpsMma * 32;  // 256 output rows
-constexpr int kDownKChunk = 128;                  // d_ff rows staged per step
+constexpr int kDownKChunk = 128;                  // d_ff columns staged per step
 constexpr int kDownHStride = kDownKChunk + 8;     // halves; padded for bank spread
 
 __device__ __forceinline__ void mma_f16(float (&d)[4], const uint4 &a, uint32_t b0, uint32_t b1) {
@@ -45,25 +43,39 @@ __device__ __forceinline__ void mma_f16(float (&d)[4], const uint4 &a, uint32_t 
         : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
 }
 
-// Shared memory: h hi/lo [2][TN][kDownHStride] fp16 + 1 int ticket flag.
-inline size_t down_mma_smem_bytes(int TN) { return size_t(2) * TN * kDownHStride * 2 + 16; }
+// Shared memory: 2 buffers x h hi/lo [TN][kDownHStride] fp16 + the ticket flag.
+inline size_t down_mma_smem_bytes(int TN) { return size_t(2) * 2 * TN * kDownHStride * 2 + 16; }
 
 template <int NT>
 __global__ void __launch_bounds__(kDownWarpsMma * 32) down_mma_kernel(const DownMmaParams p) {
     constexpr int TN = NT * 8;
+    constexpr int buf_halves = 2 * TN * kDownHStride;  // hi then lo
     extern __shared__ __align__(16) uint8_t smem[];
-    __half *h_hi = reinterpret_cast<__half *>(smem);
-    __half *h_lo = h_hi + TN * kDownHStride;
-    int *flag = reinterpret_cast<int *>(h_lo + TN * kDownHStride);
+    __half *hbuf = reinterpret_cast<__half *>(smem);
+    int *flag = reinterpret_cast<int *>(hbuf + 2 * buf_halves);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
-    const int ob = blockIdx.x;                     // 256-row output block
+    const int ob = blockIdx.x;
     const int split = blockIdx.y;
     const int k0 = split * p.kc;
     const int k1 = min(k0 + p.kc, p.F16);
-    const int mt0 = ob * (kDownRowsCta / 16) + warp * 2;  // this warp's two 16-row tiles
+    const int mt0 = ob * (kDownRowsCta / 16) + warp * 2;
     const int ksteps_row = p.F16 / 16;
+
+    auto stage = [&](int kb, int buf) {
+        __half *dst = hbuf + buf * buf_halves;
+        constexpr int vec = kDownKChunk / 8;  // 16-byte copies per token row
+        for (int i = threadIdx.x; i < 2 * TN * vec; i += blockDim.x) {
+            const int part = i / (TN * vec), r = i - part * TN * vec;
+            const int tok = r / vec, v = r - tok * vec;
+            const int k = kb + v * 8;
+            const bool ok = p.t0 + tok < p.T && k < k1;
+            const __half *src = (part ? p.h_lo : p.h_hi) + int64_t(ok ? p.t0 + tok : 0) * p.F16 + (ok ? k : 0);
+            cp_async16(dst + part * TN * kDownHStride + tok * kDownHStride + v * 8, src, ok);
+        }
+        cp_async_commit();
+    };
 
     float acc[2][NT][4];
 #pragma unroll
@@ -73,28 +85,19 @@ __global__ void __launch_bounds__(kDownWarpsMma * 32) down_mma_kernel(const Down
 #pragma unroll
             for (int e = 0; e < 4; ++e) acc[m][n][e] = 0.f;
 
-    for (int kb = k0; kb < k1; kb += kDownKChunk) {
-        const int kn = min(kDownKChunk, k1 - kb);  // multiple of 16
-        __syncthreads();
-        for (int i = threadIdx.x; i < TN * kDownKChunk; i += blockDim.x) {
-            const int tok = i / kDownKChunk, k = i - tok * kDownKChunk;
-            const int f = kb + k;
-            float hv = 0.f;
-            if (k < kn && f < p.F && p.t0 + tok < p.T) {
-                const int64_t x = int64_t(p.t0 + tok) * p.F + f;
-                float gv = p.gate_res[x], uv = p.up_res[x];
-                if (!row_flagged(p.fallback_tiles, f, p.tile_rows)) {
-                    gv += p.gate_base[x];
-                    uv += p.up_base[x];
-                }
-                hv = gv / (1.0f + expf(-gv)) * uv;
-            }
-            const __half hi = __float2half_rn(hv);
-            h_hi[tok * kDownHStride + k] = hi;
-            h_lo[tok * kDownHStride + k] = __float2half_rn(hv - __half2float(hi));
+    if (k0 < k1) stage(k0, 0);
+    int buf = 0;
+    for (int kb = k0; kb < k1; kb += kDownKChunk, buf ^= 1) {
+        if (kb + kDownKChunk < k1) {
+            stage(kb + kDownKChunk, buf ^ 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
         }
         __syncthreads();
-        const int steps = kn / 16;
+        const __half *hh = hbuf + buf * buf_halves;
+        const __half *hl = hh + TN * kDownHStride;
+        const int steps = min(kDownKChunk, k1 - kb) / 16;
 #pragma unroll 2
         for (int s = 0; s < steps; ++s) {
             const int ks = kb / 16 + s;
@@ -103,19 +106,19 @@ __global__ void __launch_bounds__(kDownWarpsMma * 32) down_mma_kernel(const Down
 #pragma unroll
             for (int n = 0; n < NT; ++n) {
                 const int off = (n * 8 + g) * kDownHStride + s * 16 + 2 * t;
-                const uint32_t bh0 = *reinterpret_cast<const uint32_t *>(h_hi + off);
-                const uint32_t bh1 = *reinterpret_cast<const uint32_t *>(h_hi + off + 8);
-                const uint32_t bl0 = *reinterpret_cast<const uint32_t *>(h_lo + off);
-                const uint32_t bl1 = *reinterpret_cast<const uint32_t *>(h_lo + off + 8);
+                const uint32_t bh0 = *reinterpret_cast<const uint32_t *>(hh + off);
+                const uint32_t bh1 = *reinterpret_cast<const uint32_t *>(hh + off + 8);
+                const uint32_t bl0 = *reinterpret_cast<const uint32_t *>(hl + off);
+                const uint32_t bl1 = *reinterpret_cast<const uint32_t *>(hl + off + 8);
                 mma_f16(acc[0][n], a0, bh0, bh1);
                 mma_f16(acc[0][n], a0, bl0, bl1);
                 mma_f16(acc[1][n], a1, bh0, bh1);
                 mma_f16(acc[1][n], a1, bl0, bl1);
             }
         }
+        __syncthreads();  // this buffer is refilled two chunks later
     }
 
-    // Split-K partials: partial[split][tok][row], tok < TN (padding tokens hold zeros).
     const int64_t slice = int64_t(TN) * p.D;
 #pragma unroll
     for (int m = 0; m < 2; ++m) {
@@ -139,7 +142,7 @@ __global__ void __launch_bounds__(kDownWarpsMma * 32) down_mma_kernel(const Down
     __syncthreads();
     if (!*flag) return;
     __threadfence();
-    // Last CTA of this output block: y[t0 + tok, o] = sum over slices in order.
+    // Last CTA of this output block: y[t0 + tok, o] = sum of the slices in order.
     const int rows_valid = min(TN, p.T - p.t0);
     for (int i = threadIdx.x; i < rows_valid * kDownRowsCta; i += blockDim.x) {
         const int tok = i / kDownRowsCta, o = ob * kDownRowsCta + (i - tok * kDownRowsCta);

@@ -68,9 +68,10 @@ struct ffnrm_ctx {
     float *partial = nullptr;            // [max_splits, 64, D] split-K partials of one token chunk
     int *tickets = nullptr;              // [D/256] split-K arrival counters (self-resetting)
     int max_splits = 64;
-    // host-streamed mode staging
-    int8_t *z_dev = nullptr;
-    float *s_dev = nullptr;
+    __half *h_hi = nullptr, *h_lo = nullptr;  // [Tm, F16] h = SiLU(g)*u as fp16 hi + lo
+    // host-streamed mode staging, double-buffered per call
+    int8_t *z_dev[2] = {nullptr, nullptr};
+    float *s_dev[2] = {nullptr, nullptr};
     float *base_dev[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};  // [slot][proj] [Tm, F]
     uint8_t *tiles_dev[2] = {nullptr, nullptr};
     uint16_t *y16_dev = nullptr;
@@ -321,9 +322,9 @@ int launch_residual_t(ffnrm_ctx *ctx, ffnrm::ResidualParams &p, cudaStream_t st)
     auto kern = ffnrm::residual_gemv_kernel<RB, TT, AH>;
     if (smem > 48 * 1024) FFNRM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
     p.row_blocks = (p.F + 31) / 32;
-    dim3 grid(unsigned(2 * p.row_blocks), unsigned((p.T + TT - 1) / TT));
+    dim3 grid(unsigned(p.row_blocks), unsigned((p.T + TT - 1) / TT));
     ProfScope prof(ctx, st, FFNRM_KERNEL_RESIDUAL);
-    kern<<<grid, ffnrm::kResWarps * 32, smem, st>>>(p);
+    kern<<<grid, 2 * ffnrm::kResWarps * 32, smem, st>>>(p);
     ctx->launches++;
     FFNRM_CUDA(cudaGetLastError());
     return FFNRM_OK;
@@ -337,15 +338,13 @@ int launch_residual_tt(ffnrm_ctx *ctx, ffnrm::ResidualParams &p, bool half, cuda
 template <int RB, int NT, bool AH, bool FB>
 int launch_residual_mma_t(ffnrm_ctx *ctx, ffnrm::ResidualParams &p, cudaStream_t st) {
     constexpr int TN = NT * 8;
-    const size_t smem = ffnrm::residual_mma_smem_bytes(TN, p.G, FB);
+    const size_t smem = ffnrm::residual_mma_smem_bytes<RB, AH>(TN, p.G, FB);
     auto kern = ffnrm::residual_mma_kernel<RB, NT, AH, FB>;
     if (smem > 48 * 1024) FFNRM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-    constexpr int warps = 4;
     p.row_blocks = (p.F + 31) / 32;
-    const int per_proj = (p.row_blocks + warps - 1) / warps;
-    dim3 grid(unsigned(2 * per_proj), unsigned((p.T + TN - 1) / TN));
+    dim3 grid(unsigned((p.row_blocks + 1) / 2), unsigned((p.T + TN - 1) / TN));
     ProfScope prof(ctx, st, FFNRM_KERNEL_RESIDUAL);
-    kern<<<grid, warps * 32, smem, st>>>(p);
+    kern<<<grid, 128, smem, st>>>(p);
     ctx->launches++;
     FFNRM_CUDA(cudaGetLastError());
     return FFNRM_OK;
@@ -369,8 +368,11 @@ int launch_residual_rb(ffnrm_ctx *ctx, ffnrm::ResidualParams &p, bool half, cuda
     return launch_residual_mma_nt<RB, 4>(ctx, p, half, st);  // 32-token tiles (64 would spill)
 }
 
+// Residual contraction of both projections. Residual mode (gate_base == nullptr): writes
+// gate_res/up_res. Forward mode: merges with the base sums and writes h into the workspace.
 int enqueue_residual(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s, int T, float *gate_res,
-                     float *up_res, int32_t *dots, const uint8_t *tiles, cudaStream_t st) {
+                     float *up_res, int32_t *dots, const uint8_t *tiles, const float *gate_base,
+                     const float *up_base, cudaStream_t st) {
     LayerDev &L = ctx->layers[size_t(layer)];
     if (tiles && !L.has_fallback)
         return fail(FFNRM_ERR_STATE, "fallback tiles given but layer %d was loaded without fallback data", layer);
@@ -383,6 +385,11 @@ int enqueue_residual(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s,
     p.out[0] = gate_res;
     p.out[1] = up_res;
     p.dots = dots;
+    p.base[0] = gate_base;
+    p.base[1] = up_base;
+    p.h_hi = gate_base ? ctx->h_hi : nullptr;
+    p.h_lo = gate_base ? ctx->h_lo : nullptr;
+    p.F16 = (ctx->cfg.d_ff + 15) / 16 * 16;
     p.fallback_tiles = tiles;
     p.F = ctx->cfg.d_ff;
     p.D = ctx->cfg.d_model;
@@ -409,29 +416,23 @@ int launch_down_t(ffnrm_ctx *ctx, ffnrm::DownMmaParams &p, dim3 grid, cudaStream
     return FFNRM_OK;
 }
 
-int enqueue_down(ffnrm_ctx *ctx, int layer, int T, const float *gate_base, const float *up_base,
-                 const uint8_t *tiles, float *y32, uint16_t *y16, cudaStream_t st) {
+int enqueue_down(ffnrm_ctx *ctx, int layer, int T, float *y32, uint16_t *y16, cudaStream_t st) {
     LayerDev &L = ctx->layers[size_t(layer)];
     const int F = ctx->cfg.d_ff, D = ctx->cfg.d_model;
     const int F16 = (F + 15) / 16 * 16;
     ffnrm::DownMmaParams p{};
-    p.gate_res = ctx->res[0];
-    p.up_res = ctx->res[1];
-    p.gate_base = gate_base;
-    p.up_base = up_base;
-    p.fallback_tiles = tiles;
+    p.h_hi = ctx->h_hi;
+    p.h_lo = ctx->h_lo;
     p.down_frag = static_cast<const uint4 *>(L.down.ptr);
     p.partial = ctx->partial;
     p.tickets = ctx->tickets;
     p.y32 = y32;
     p.y16 = reinterpret_cast<__half *>(y16);
-    p.F = F;
     p.F16 = F16;
     p.D = D;
     p.T = T;
-    p.tile_rows = ctx->cfg.base_tile_rows;
     const int oblocks = D / ffnrm::kDownRowsCta;
-    // ~2 CTAs per SM; slices are multiples of 16 rows of d_ff.
+    // ~2 CTAs per SM; slices are multiples of 16 columns of d_ff.
     int splits = std::max(1, std::min(ctx->max_splits, (2 * ctx->num_sms + oblocks - 1) / oblocks));
     int kc = (F16 + splits - 1) / splits;
     kc = (kc + 15) / 16 * 16;
@@ -478,17 +479,20 @@ int ffnrm_create(ffnrm_ctx **out, int device, const ffnrm_config *cfg) {
     ctx->layers.resize(size_t(c.n_layers));
     cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
     const size_t TF = size_t(c.max_tokens) * c.d_ff, TD = size_t(c.max_tokens) * c.d_model;
+    const size_t F16 = (size_t(c.d_ff) + 15) / 16 * 16;
     const int ntiles = (c.d_ff + c.base_tile_rows - 1) / c.base_tile_rows;
     bool ok = cudaMalloc(&ctx->res[0], TF * 4) == cudaSuccess && cudaMalloc(&ctx->res[1], TF * 4) == cudaSuccess &&
               cudaMalloc(&ctx->partial, size_t(ctx->max_splits) * 64 * c.d_model * 4) == cudaSuccess &&
               cudaMalloc(&ctx->tickets, size_t(c.d_model / 256) * sizeof(int)) == cudaSuccess &&
               cudaMemset(ctx->tickets, 0, size_t(c.d_model / 256) * sizeof(int)) == cudaSuccess &&
-              cudaMalloc(&ctx->z_dev, TD) == cudaSuccess &&
-              cudaMalloc(&ctx->s_dev, size_t(c.max_tokens) * ctx->G * 4) == cudaSuccess &&
+              cudaMalloc(&ctx->h_hi, size_t(c.max_tokens) * F16 * 2) == cudaSuccess &&
+              cudaMalloc(&ctx->h_lo, size_t(c.max_tokens) * F16 * 2) == cudaSuccess &&
               cudaMalloc(&ctx->y16_dev, TD * 2) == cudaSuccess;
     for (int sl = 0; sl < 2 && ok; ++sl) {
         ok = cudaMalloc(&ctx->base_dev[sl][0], TF * 4) == cudaSuccess && cudaMalloc(&ctx->base_dev[sl][1], TF * 4) == cudaSuccess &&
-             cudaMalloc(&ctx->tiles_dev[sl], size_t(ntiles)) == cudaSuccess;
+             cudaMalloc(&ctx->tiles_dev[sl], size_t(ntiles)) == cudaSuccess &&
+             cudaMalloc(&ctx->z_dev[sl], TD) == cudaSuccess &&
+             cudaMalloc(&ctx->s_dev[sl], size_t(c.max_tokens) * ctx->G * 4) == cudaSuccess;
     }
     ok = ok && cudaStreamCreateWithFlags(&ctx->copy_stream, cudaStreamNonBlocking) == cudaSuccess;
     for (int sl = 0; sl < 2 && ok; ++sl)
@@ -512,13 +516,15 @@ int ffnrm_destroy(ffnrm_ctx *ctx) {
     cudaFree(ctx->res[1]);
     cudaFree(ctx->partial);
     cudaFree(ctx->tickets);
-    cudaFree(ctx->z_dev);
-    cudaFree(ctx->s_dev);
+    cudaFree(ctx->h_hi);
+    cudaFree(ctx->h_lo);
     cudaFree(ctx->y16_dev);
     for (int sl = 0; sl < 2; ++sl) {
         cudaFree(ctx->base_dev[sl][0]);
         cudaFree(ctx->base_dev[sl][1]);
         cudaFree(ctx->tiles_dev[sl]);
+        cudaFree(ctx->z_dev[sl]);
+        cudaFree(ctx->s_dev[sl]);
         if (ctx->base_ready[sl]) cudaEventDestroy(ctx->base_ready[sl]);
         if (ctx->slot_free[sl]) cudaEventDestroy(ctx->slot_free[sl]);
     }
@@ -590,8 +596,8 @@ int ffnrm_residual(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s, i
     if (!aligned(z, 16) || !aligned(s, 4) || !aligned(gate_res, 4) || !aligned(up_res, 4) || !aligned(group_dots, 8))
         return fail(FFNRM_ERR_ARG, "z must be 16-byte aligned and s/outputs 4-byte aligned (dots 8-byte)");
     DeviceGuard guard(ctx->device);
-    return enqueue_residual(ctx, layer, z, s, tokens, gate_res, up_res, group_dots, fallback_tiles,
-                            static_cast<cudaStream_t>(stream));
+    return enqueue_residual(ctx, layer, z, s, tokens, gate_res, up_res, group_dots, fallback_tiles, nullptr,
+                            nullptr, static_cast<cudaStream_t>(stream));
 }
 
 int ffnrm_ffn_forward(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s, int tokens, const float *gate_base,
@@ -608,8 +614,10 @@ int ffnrm_ffn_forward(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s
         return fail(FFNRM_ERR_ARG, "z must be 16-byte aligned and s, base sums and outputs element-aligned");
     DeviceGuard guard(ctx->device);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if ((rc = enqueue_residual(ctx, layer, z, s, tokens, ctx->res[0], ctx->res[1], nullptr, fallback_tiles, st))) return rc;
-    return enqueue_down(ctx, layer, tokens, gate_base, up_base, fallback_tiles, y_f32, y_f16, st);
+    if ((rc = enqueue_residual(ctx, layer, z, s, tokens, nullptr, nullptr, nullptr, fallback_tiles, gate_base, up_base,
+                               st)))
+        return rc;
+    return enqueue_down(ctx, layer, tokens, y_f32, y_f16, st);
 }
 
 int ffnrm_ffn_forward_host(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s, int tokens,
@@ -626,26 +634,26 @@ int ffnrm_ffn_forward_host(ffnrm_ctx *ctx, int layer, const int8_t *z, const flo
     const int sl = ctx->slot;
     ctx->slot ^= 1;
     const size_t tf_bytes = size_t(tokens) * F * 4;
-    // Activations on the compute stream (needed first by the residual contraction).
-    FFNRM_CUDA(cudaMemcpyAsync(ctx->z_dev, z, size_t(tokens) * D, cudaMemcpyHostToDevice, st));
-    FFNRM_CUDA(cudaMemcpyAsync(ctx->s_dev, s, size_t(tokens) * G * 4, cudaMemcpyHostToDevice, st));
+    cudaStream_t cs = ctx->copy_stream;
+    // Every upload goes on the copy stream into slot `sl`, which the call before the
+    // previous one has released; the next layer's upload thus overlaps this layer's kernels.
+    FFNRM_CUDA(cudaStreamWaitEvent(cs, ctx->slot_free[sl], 0));
+    FFNRM_CUDA(cudaMemcpyAsync(ctx->z_dev[sl], z, size_t(tokens) * D, cudaMemcpyHostToDevice, cs));
+    FFNRM_CUDA(cudaMemcpyAsync(ctx->s_dev[sl], s, size_t(tokens) * G * 4, cudaMemcpyHostToDevice, cs));
     const uint8_t *tiles_dev = nullptr;
     if (fallback_tiles) {
         const int ntiles = (F + ctx->cfg.base_tile_rows - 1) / ctx->cfg.base_tile_rows;
-        FFNRM_CUDA(cudaMemcpyAsync(ctx->tiles_dev[sl], fallback_tiles, size_t(ntiles), cudaMemcpyHostToDevice, st));
+        FFNRM_CUDA(cudaMemcpyAsync(ctx->tiles_dev[sl], fallback_tiles, size_t(ntiles), cudaMemcpyHostToDevice, cs));
         tiles_dev = ctx->tiles_dev[sl];
     }
-    // Base sums on the copy stream, into a slot no earlier call is still reading.
-    FFNRM_CUDA(cudaStreamWaitEvent(ctx->copy_stream, ctx->slot_free[sl], 0));
-    FFNRM_CUDA(cudaMemcpyAsync(ctx->base_dev[sl][0], gate_base, tf_bytes, cudaMemcpyHostToDevice, ctx->copy_stream));
-    FFNRM_CUDA(cudaMemcpyAsync(ctx->base_dev[sl][1], up_base, tf_bytes, cudaMemcpyHostToDevice, ctx->copy_stream));
-    FFNRM_CUDA(cudaEventRecord(ctx->base_ready[sl], ctx->copy_stream));
-    if ((rc = enqueue_residual(ctx, layer, ctx->z_dev, ctx->s_dev, tokens, ctx->res[0], ctx->res[1], nullptr, tiles_dev, st)))
-        return rc;
+    FFNRM_CUDA(cudaMemcpyAsync(ctx->base_dev[sl][0], gate_base, tf_bytes, cudaMemcpyHostToDevice, cs));
+    FFNRM_CUDA(cudaMemcpyAsync(ctx->base_dev[sl][1], up_base, tf_bytes, cudaMemcpyHostToDevice, cs));
+    FFNRM_CUDA(cudaEventRecord(ctx->base_ready[sl], cs));
     FFNRM_CUDA(cudaStreamWaitEvent(st, ctx->base_ready[sl], 0));
-    if ((rc = enqueue_down(ctx, layer, tokens, ctx->base_dev[sl][0], ctx->base_dev[sl][1], tiles_dev, nullptr,
-                           ctx->y16_dev, st)))
+    if ((rc = enqueue_residual(ctx, layer, ctx->z_dev[sl], ctx->s_dev[sl], tokens, nullptr, nullptr, nullptr, tiles_dev,
+                               ctx->base_dev[sl][0], ctx->base_dev[sl][1], st)))
         return rc;
+    if ((rc = enqueue_down(ctx, layer, tokens, nullptr, ctx->y16_dev, st))) return rc;
     FFNRM_CUDA(cudaEventRecord(ctx->slot_free[sl], st));
     FFNRM_CUDA(cudaMemcpyAsync(y_f16, ctx->y16_dev, size_t(tokens) * D * 2, cudaMemcpyDeviceToHost, st));
     return FFNRM_OK;

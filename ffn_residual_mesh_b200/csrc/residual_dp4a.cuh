@@ -1,15 +1,18 @@
 // Decode residual contraction on CUDA cores: exact int32 group dots with __dp4a,
-// gate and up in one launch, lane-per-row.
+// gate and up of the same rows in one CTA, lane-per-row.
 //
 // Replaces residual_kernel (src/exact_residual_cuda_runner.cu:122-159), which
 // evaluates q*alpha*z*s per element in fp32 with byte loads and a shared-memory
-// tree. Here a CTA owns one 32-row block of one projection: lane l owns row
-// 32*rb + l, the CTA's warps split the d_model groups, and every warp-wide load reads
-// 32 consecutive 16-byte code records (512 B, fully coalesced). Activations sit in
-// shared memory in natural order and are read as broadcasts, so no warp reduction is
-// needed; each group dot is exact in int32 before alpha[row,g]*s[t,g] is applied in
-// fp32. Partial sums of the warps meet in shared memory in a fixed order. Rows of
-// flagged fallback tiles compute sum_g s*(alpha*(P01 + 4 P23) + beta*zsum) instead.
+// tree. Here a CTA owns one 32-row block of both projections: lane l owns row
+// 32*rb + l; warps 0-3 take the gate rows and 4-7 the up rows, each splitting the
+// d_model groups four ways, and every warp-wide load reads 32 consecutive 16-byte
+// code records (512 B, fully coalesced). Activations sit in shared memory in natural
+// order and are read as broadcasts, so no warp reduction is needed; each group dot is
+// exact in int32 before alpha[row,g]*s[t,g] is applied in fp32. Partial sums of the
+// warps meet in shared memory in a fixed order. Rows of flagged fallback tiles compute
+// sum_g s*(alpha*(P01 + 4 P23) + beta*zsum) instead. In forward mode the CTA then
+// merges both projections with the base sums and writes h = SiLU(g)*u for the down
+// projection (the merge of src/exact_cpu_base_gpu_full_ffn_runner.cu:225-227).
 #pragma once
 
 #include "ffnrm_common.cuh"
@@ -20,23 +23,45 @@ struct ResidualParams {
     ProjView proj[2];
     const int8_t *z;      // [T, D]
     const float *s;       // [T, G]
-    float *out[2];        // [T, F]
+    float *out[2];        // [T, F] (residual mode) or null
     int32_t *dots;        // [2, T, F, G] or null
     const uint8_t *fallback_tiles;
-    int F, D, G, T, tile_rows;
+    // forward mode: merge with the base sums and write h = SiLU(g)*u as fp16 hi + lo
+    const float *base[2];  // [T, F]
+    __half *h_hi, *h_lo;   // [T, F16], F16 = F rounded up to 16 (padding columns written as 0)
+    int F, D, G, T, tile_rows, F16;
     int row_blocks;       // ceil(F / 32)
 };
 
-constexpr int kResWarps = 4;
+// h = g/(1+exp(-g))*u for one (token, row); flagged rows ignore the base (their g/u
+// already are the unsplit projections). Writes fp16 hi and lo = fp16(h - hi).
+__device__ __forceinline__ void store_h(const ResidualParams &p, int tok, int row, float g, float u, bool flagged) {
+    const int64_t i = int64_t(tok) * p.F16 + row;
+    if (row >= p.F) {
+        p.h_hi[i] = __float2half_rn(0.f);
+        p.h_lo[i] = __float2half_rn(0.f);
+        return;
+    }
+    if (!flagged) {
+        g += p.base[0][int64_t(tok) * p.F + row];
+        u += p.base[1][int64_t(tok) * p.F + row];
+    }
+    const float h = g / (1.0f + expf(-g)) * u;
+    const __half hi = __float2half_rn(h);
+    p.h_hi[i] = hi;
+    p.h_lo[i] = __float2half_rn(h - __half2float(hi));
+}
 
-// Shared memory: [z TT*D int8][s TT*G f32][zsum TT*G f32][red kResWarps*TT*32 f32]
+constexpr int kResWarps = 4;  // per projection; the CTA runs 2 * kResWarps warps
+
+// Shared memory: [z TT*D int8][s TT*G f32][zsum TT*G f32][red 2*kResWarps*TT*32 f32]
 inline size_t residual_smem_bytes(int TT, int D) {
     const int G = D / 32;
-    return size_t(TT) * D + size_t(TT) * G * 8 + size_t(kResWarps) * TT * 32 * 4;
+    return size_t(TT) * D + size_t(TT) * G * 8 + size_t(2 * kResWarps) * TT * 32 * 4;
 }
 
 template <int RB, int TT, bool AHALF>
-__global__ void __launch_bounds__(kResWarps * 32) residual_gemv_kernel(const ResidualParams p) {
+__global__ void __launch_bounds__(2 * kResWarps * 32) residual_gemv_kernel(const ResidualParams p) {
     extern __shared__ __align__(16) uint8_t smem[];
     const int G = p.G, D = p.D, F = p.F, T = p.T;
     int8_t *z_sm = reinterpret_cast<int8_t *>(smem);
@@ -44,8 +69,7 @@ __global__ void __launch_bounds__(kResWarps * 32) residual_gemv_kernel(const Res
     float *zsum_sm = s_sm + TT * G;
     float *red = zsum_sm + TT * G;
 
-    const int proj = blockIdx.x / p.row_blocks;
-    const int rb = blockIdx.x - proj * p.row_blocks;
+    const int rb = blockIdx.x;
     const int t0 = blockIdx.y * TT;
 
     // Stage TT tokens of activations (16-byte copies) and their group scales.
@@ -74,12 +98,13 @@ __global__ void __launch_bounds__(kResWarps * 32) residual_gemv_kernel(const Res
     __syncthreads();
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int proj = warp / kResWarps, wk = warp - proj * kResWarps;
     const int row = rb * 32 + lane;
     const bool valid = row < F;
     const bool flagged = valid && row_flagged(p.fallback_tiles, row, p.tile_rows);
     const ProjView pv = p.proj[proj];
     const int C = G / 2;
-    const int c_begin = warp * C / kResWarps, c_end = (warp + 1) * C / kResWarps;
+    const int c_begin = wk * C / kResWarps, c_end = (wk + 1) * C / kResWarps;
 
     float acc[TT];
 #pragma unroll
@@ -132,12 +157,27 @@ __global__ void __launch_bounds__(kResWarps * 32) residual_gemv_kernel(const Res
 #pragma unroll
     for (int t = 0; t < TT; ++t) red[(warp * TT + t) * 32 + lane] = acc[t];
     __syncthreads();
-    if (warp == 0 && valid) {
+    if (p.h_hi != nullptr) {
+        // forward mode: warp 0 merges gate and up of its 32 rows and writes h
+        if (warp == 0 && row < p.F16) {
+#pragma unroll
+            for (int t = 0; t < TT; ++t) {
+                if (t0 + t >= T) continue;
+                float gv = 0.f, uv = 0.f;
+#pragma unroll
+                for (int w = 0; w < kResWarps; ++w) {
+                    gv += red[(w * TT + t) * 32 + lane];
+                    uv += red[((kResWarps + w) * TT + t) * 32 + lane];
+                }
+                store_h(p, t0 + t, row, gv, uv, flagged);
+            }
+        }
+    } else if (wk == 0 && valid) {
 #pragma unroll
         for (int t = 0; t < TT; ++t) {
             float v = 0.f;
 #pragma unroll
-            for (int w = 0; w < kResWarps; ++w) v += red[(w * TT + t) * 32 + lane];
+            for (int w = 0; w < kResWarps; ++w) v += red[((proj * kResWarps + w) * TT + t) * 32 + lane];
             if (t0 + t < T) p.out[proj][int64_t(t0 + t) * F + row] = v;
         }
     }
