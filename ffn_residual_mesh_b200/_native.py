@@ -12,7 +12,7 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "lib" / "libffnrm.so"
 
-OK, ERR_ARG, ERR_CUDA, ERR_STATE, ERR_NOMEM = 0, 1, 2, 3, 4
+OK, ERR_ARG, ERR_CUDA, ERR_STATE, ERR_NOMEM, ERR_TIMEOUT = 0, 1, 2, 3, 4, 5
 CODES_Q4_BYTES, CODES_QLO2_ROWPACKED, CODES_BITPLANES = 0, 1, 2
 KERNEL_RESIDUAL, KERNEL_DOWN, KERNEL_REDUCE = 0, 1, 2
 
@@ -32,6 +32,7 @@ SIGNATURES = {
     "ffnrm_cast_f16": (c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
     "ffnrm_layer_bytes": (c_int, [c_void_p, c_int, POINTER(c_int64), POINTER(c_int64)]),
     "ffnrm_launch_count": (c_int64, [c_void_p]),
+    "ffnrm_check_device_error": (c_int, [c_void_p, c_void_p]),
     "ffnrm_profile_enable": (c_int, [c_void_p, c_int]),
     "ffnrm_profile_read": (c_int, [c_void_p, c_int, POINTER(ctypes.c_double), POINTER(c_int64)]),
     "ffnrm_last_error": (c_char_p, []),
@@ -82,4 +83,6 @@ def check(rc: int) -> None:
         raise ValueError(msg)
     if rc == ERR_NOMEM:
         raise MemoryError(msg)
+    if rc == ERR_TIMEOUT:
+        raise TimeoutError(msg)
     raise RuntimeError(f"ffnrm error {rc}: {msg}")

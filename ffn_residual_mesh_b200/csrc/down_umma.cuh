@@ -1,0 +1,181 @@
+// fp16 down projection on the 5th-generation tensor cores (tcgen05, TMEM accumulator).
+//
+// Replaces swiglu_down_kernel (src/exact_cpu_base_gpu_full_ffn_runner.cu:217-240) and
+// the torch.mm down of scripts/benchmark_gpu_full_ffn_density.py:162. The merge and
+// SwiGLU already happened in the residual kernel, which wrote h = SiLU(g)*u as two
+// fp16 parts (h = hi + lo to ~2^-22 relative), so y keeps fp32-level accuracy.
+//
+// y[t, o] = sum_f h[t, f] * Wd[o, f] is a GEMM with M = d_model (down rows), N = tokens,
+// K = d_ff. CTA tile: 128 down rows x N tokens x a split-K slice of d_ff.
+//   warp 0 / lane 0 : TMA producer. Per 64-column K step it loads the 128x64 fp16 tile of
+//                     Wd and the Nx64 tiles of h hi and lo (128-byte swizzle) into a
+//                     kStages-deep shared-memory ring, completing on full[s].
+//   warp 1 / lane 0 : MMA issuer. Per stage, 4 K=16 steps x (hi, lo) tcgen05.mma into one
+//                     128xN f32 accumulator in tensor memory; tcgen05.commit frees the stage.
+//   warps 0-3       : epilogue. Each warp reads its 32 TMEM lanes (down rows) with
+//                     tcgen05.ld and writes y directly (one slice) or a split-K partial;
+//                     the last CTA of an output tile (atomic ticket) sums the partials
+//                     in slice order (deterministic).
+// Every mbarrier wait is bounded; on timeout the kernel records an error code in
+// p.err, drains its outstanding copies, frees its TMEM and returns.
+#pragma once
+
+#include <cuda_fp16.h>
+
+#include "ffnrm_common.cuh"
+#include "sm100.cuh"
+
+namespace ffnrm {
+
+struct DownUmmaParams {
+    float *partial;  // [splits][T][D] (split-K only)
+    int *tickets;    // [D/128][ceil(T/N)] zero-initialised, self-resetting
+    float *y32;      // [T, D] or null
+    __half *y16;     // [T, D] or null
+    int *err;        // error word (bounded waits)
+    int D, F16, T, splits, kc;  // kc: d_ff columns per slice, a multiple of 64
+};
+
+constexpr int kUmmaM = 128;
+constexpr int kUmmaK = 64;  // d_ff columns per stage (one 128-byte swizzle row)
+
+template <int N>
+struct DownUmmaCfg {
+    static constexpr int stages = N <= 16 ? 5 : (N <= 32 ? 4 : (N <= 64 ? 3 : 4));
+    static constexpr int a_bytes = kUmmaM * kUmmaK * 2;  // 16 KB
+    static constexpr int b_bytes = N * kUmmaK * 2;       // per part (hi or lo)
+    static constexpr int stage_bytes = a_bytes + 2 * b_bytes;
+    static constexpr int tmem_cols = N < 32 ? 32 : N;
+    static constexpr size_t smem = size_t(stages) * stage_bytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+template <int N>
+__global__ void __launch_bounds__(128, 1) down_umma_kernel(const __grid_constant__ CUtensorMap tm_w,
+                                                           const __grid_constant__ CUtensorMap tm_hi,
+                                                           const __grid_constant__ CUtensorMap tm_lo,
+                                                           const DownUmmaParams p) {
+    using Cfg = DownUmmaCfg<N>;
+    constexpr int S = Cfg::stages;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *tiles = smem;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + S * Cfg::stage_bytes);
+    uint64_t *empty = full + S;
+    uint64_t *done = empty + S;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+    int *flag = reinterpret_cast<int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * kUmmaM;
+    const int nt = blockIdx.y;
+    const int t0 = nt * N;
+    const int split = blockIdx.z;
+    const int k0 = split * p.kc;
+    const int k1 = min(k0 + p.kc, p.F16);
+    const int nk = (k1 - k0 + kUmmaK - 1) / kUmmaK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            sm100::mbar_init(full + s, 1);
+            sm100::mbar_init(empty + s, 1);
+        }
+        sm100::mbar_init(done, 1);
+        sm100::fence_barrier_init();
+    }
+    if (warp == 0) sm100::tmem_alloc(tmem_slot, Cfg::tmem_cols);
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        // TMA producer
+        int issued = 0;
+        for (int it = 0; it < nk; ++it) {
+            const int s = it % S;
+            if (!sm100::mbar_wait(empty + s, ((it / S) & 1) ^ 1, p.err, sm100::kErrWaitEmpty)) break;
+            uint8_t *st = tiles + s * Cfg::stage_bytes;
+            sm100::mbar_arrive_expect_tx(full + s, Cfg::stage_bytes);
+            const int kx = k0 + it * kUmmaK;
+            sm100::tma_load_2d(st, &tm_w, kx, m0, full + s);
+            sm100::tma_load_2d(st + Cfg::a_bytes, &tm_hi, kx, t0, full + s);
+            sm100::tma_load_2d(st + Cfg::a_bytes + Cfg::b_bytes, &tm_lo, kx, t0, full + s);
+            ++issued;
+        }
+        // No copy may still be in flight when the CTA exits: wait for the last stages.
+        for (int it = max(0, issued - S); it < issued; ++it)
+            sm100::mbar_wait(full + it % S, (it / S) & 1, p.err, sm100::kErrWaitFull);
+    } else if (warp == 1 && lane == 0) {
+        // MMA issuer
+        constexpr uint32_t idesc = sm100::umma_idesc_f16_f32(kUmmaM, N);
+        for (int it = 0; it < nk; ++it) {
+            const int s = it % S;
+            if (!sm100::mbar_wait(full + s, (it / S) & 1, p.err, sm100::kErrWaitFull)) break;
+            sm100::tc_fence_after();
+            const uint32_t a = sm100::smem_u32(tiles + s * Cfg::stage_bytes);
+            const uint32_t bh = a + Cfg::a_bytes, bl = bh + Cfg::b_bytes;
+#pragma unroll
+            for (int k = 0; k < kUmmaK / 16; ++k) {
+                const uint64_t ad = sm100::umma_desc_sw128(a + 32 * k);
+                sm100::umma_f16(tmem, ad, sm100::umma_desc_sw128(bh + 32 * k), idesc, (it | k) != 0);
+                sm100::umma_f16(tmem, ad, sm100::umma_desc_sw128(bl + 32 * k), idesc, 1);
+            }
+            sm100::umma_commit(empty + s);  // the stage is free once these MMAs finish
+        }
+        sm100::umma_commit(done);
+    }
+    __syncwarp();
+
+    // Epilogue: wait for the accumulator, then each warp drains its 32 TMEM lanes.
+    const bool ok = sm100::mbar_wait(done, 0, p.err, sm100::kErrWaitDone);
+    sm100::tc_fence_after();
+    const int row = m0 + warp * 32 + lane;
+    const bool direct = p.splits == 1;
+    float *dst = direct ? nullptr : p.partial + int64_t(split) * p.T * p.D;
+    if (ok) {
+#pragma unroll
+        for (int c = 0; c < N; c += 16) {
+            uint32_t r[16];
+            sm100::tmem_ld16(tmem + (uint32_t(warp * 32) << 16) + c, r);
+            sm100::tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const int tok = t0 + c + j;
+                if (tok >= p.T) break;
+                const float v = __uint_as_float(r[j]);
+                const int64_t yi = int64_t(tok) * p.D + row;
+                if (direct) {
+                    if (p.y32) p.y32[yi] = v;
+                    if (p.y16) p.y16[yi] = __float2half_rn(v);
+                } else {
+                    dst[yi] = v;
+                }
+            }
+        }
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) sm100::tmem_dealloc(tmem, Cfg::tmem_cols);
+    if (direct || !ok) return;
+
+    // split-K: the last CTA of this (row tile, token tile) sums the slices in order
+    __threadfence();
+    __syncthreads();
+    int *ticket = p.tickets + blockIdx.x * gridDim.y + nt;
+    if (threadIdx.x == 0) *flag = atomicAdd(ticket, 1) == p.splits - 1;
+    __syncthreads();
+    if (!*flag) return;
+    __threadfence();
+    const int ntok = min(N, p.T - t0);
+    for (int i = threadIdx.x; i < ntok * kUmmaM; i += blockDim.x) {
+        const int tok = t0 + i / kUmmaM, o = m0 + (i % kUmmaM);
+        const int64_t yi = int64_t(tok) * p.D + o;
+        float v = 0.f;
+        for (int sp = 0; sp < p.splits; ++sp) v += __ldcg(p.partial + int64_t(sp) * p.T * p.D + yi);
+        if (p.y32) p.y32[yi] = v;
+        if (p.y16) p.y16[yi] = __float2half_rn(v);
+    }
+    if (threadIdx.x == 0) *ticket = 0;  // ready for the next launch on this stream
+}
+
+}  // namespace ffnrm

@@ -5,6 +5,7 @@
 // non-blocking copy stream plus events for the host-streamed base pipeline.
 #include "ffnrm.h"
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -17,7 +18,7 @@
 #include <string>
 #include <vector>
 
-#include "down_mma.cuh"
+#include "down_umma.cuh"
 #include "ffnrm_common.cuh"
 #include "residual_dp4a.cuh"
 #include "residual_mma.cuh"
@@ -54,7 +55,38 @@ struct LayerDev {
     bool scales_half = true;
     bool has_fallback = false;
     DevBuf pair[2], plane[2], pair_hi[2], alpha[2], beta[2], down;
+    CUtensorMap down_map;  // TMA view of down [D][F16] fp16, box 64 x 128, 128-byte swizzle
 };
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = [] {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            ptr = nullptr;
+        return reinterpret_cast<EncodeTiledFn>(ptr);
+    }();
+    return fn;
+}
+
+// 2-D fp16 tensor [rows][cols] (row stride ld elements) viewed in boxes of 64 columns x box_rows
+// rows with 128-byte swizzle; out-of-range elements read as zero.
+bool make_fp16_map(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows, uint64_t ld, uint32_t box_rows) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {ld * 2};
+    const cuuint32_t box[2] = {64, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 }  // namespace
 
@@ -65,9 +97,12 @@ struct ffnrm_ctx {
     std::vector<LayerDev> layers;
     // workspace
     float *res[2] = {nullptr, nullptr};  // [Tm, F]
-    float *partial = nullptr;            // [max_splits, 64, D] split-K partials of one token chunk
-    int *tickets = nullptr;              // [D/256] split-K arrival counters (self-resetting)
+    float *partial = nullptr;            // split-K partials, kPartialFloats floats
+    int *tickets = nullptr;              // [D/128][ceil(Tm/16)] split-K arrival counters (self-resetting)
+    int *err = nullptr;                  // device error word written by bounded waits
+    CUtensorMap h_map[4][2];             // h hi/lo views for token tiles 16, 32, 64, 128
     int max_splits = 64;
+    static constexpr size_t kPartialFloats = size_t(2) * 160 * 128 * 128;  // >= splits*T*D whenever splits > 1
     __half *h_hi = nullptr, *h_lo = nullptr;  // [Tm, F16] h = SiLU(g)*u as fp16 hi + lo
     // host-streamed mode staging, double-buffered per call
     int8_t *z_dev[2] = {nullptr, nullptr};
@@ -235,24 +270,12 @@ int upload_scales(DevBuf &b, const float *v, int64_t F, int64_t G, bool as_half)
     return upload(b, h.data(), size_t(n) * 2);
 }
 
-// fp16 down [D, ld] (F used columns) -> fragment-native [D/16][F16/16][32 lanes][4 words]:
-// lane 4g+t holds (row g, k 2t..2t+1), (row g+8, k 2t..), (row g, k 2t+8..), (row g+8, k 2t+8..)
-// of each 16x16 tile, the m16n8k16 A registers. Columns F..F16-1 are zero.
+// fp16 down [D, ld] (F used columns) -> row-major [D][F16] with zero columns F..F16-1.
 int upload_down(DevBuf &b, const uint16_t *down, int64_t ld, int64_t F, int64_t D) {
-    const int64_t F16 = (F + 15) / 16 * 16, KS = F16 / 16;
-    std::vector<uint16_t> fr(size_t(D * F16), 0);
-    auto at = [&](int64_t o, int64_t k) -> uint16_t { return k < F ? down[o * ld + k] : uint16_t(0); };
-    for (int64_t mt = 0; mt < D / 16; ++mt)
-        for (int64_t ks = 0; ks < KS; ++ks)
-            for (int lane = 0; lane < 32; ++lane) {
-                const int64_t g = lane / 4, t = lane % 4, r = mt * 16 + g, k = ks * 16 + 2 * t;
-                uint16_t *w = fr.data() + ((mt * KS + ks) * 32 + lane) * 8;
-                w[0] = at(r, k), w[1] = at(r, k + 1);
-                w[2] = at(r + 8, k), w[3] = at(r + 8, k + 1);
-                w[4] = at(r, k + 8), w[5] = at(r, k + 9);
-                w[6] = at(r + 8, k + 8), w[7] = at(r + 8, k + 9);
-            }
-    return upload(b, fr.data(), fr.size() * 2);
+    const int64_t F16 = (F + 15) / 16 * 16;
+    std::vector<uint16_t> rm(size_t(D * F16), 0);
+    for (int64_t o = 0; o < D; ++o) std::memcpy(rm.data() + o * F16, down + o * ld, size_t(F) * 2);
+    return upload(b, rm.data(), rm.size() * 2);
 }
 
 void free_layer(LayerDev &L) {
@@ -404,13 +427,23 @@ int enqueue_residual(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s,
     }
 }
 
-template <int NT>
-int launch_down_t(ffnrm_ctx *ctx, ffnrm::DownMmaParams &p, dim3 grid, cudaStream_t st) {
-    const size_t smem = ffnrm::down_mma_smem_bytes(NT * 8);
-    auto kern = ffnrm::down_mma_kernel<NT>;
-    if (smem > 48 * 1024) FFNRM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+template <int N>
+int launch_down_t(ffnrm_ctx *ctx, const CUtensorMap &wmap, int map_idx, ffnrm::DownUmmaParams &p, cudaStream_t st) {
+    using Cfg = ffnrm::DownUmmaCfg<N>;
+    auto kern = ffnrm::down_umma_kernel<N>;
+    FFNRM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::smem)));
+    const int occ = Cfg::smem <= 113 * 1024 ? 2 : 1;
+    const int mt = p.D / ffnrm::kUmmaM, ntile = (p.T + N - 1) / N;
+    const int ksteps = (p.F16 + ffnrm::kUmmaK - 1) / ffnrm::kUmmaK;
+    int splits = std::max(1, std::min(ksteps, occ * ctx->num_sms / (mt * ntile)));
+    const int kc_steps = (ksteps + splits - 1) / splits;
+    splits = (ksteps + kc_steps - 1) / kc_steps;
+    if (splits > 1 && size_t(splits) * p.T * p.D > ffnrm_ctx::kPartialFloats) splits = 1, p.kc = ksteps * ffnrm::kUmmaK;
+    p.splits = splits;
+    p.kc = splits == 1 ? ksteps * ffnrm::kUmmaK : kc_steps * ffnrm::kUmmaK;
+    const dim3 grid{unsigned(mt), unsigned(ntile), unsigned(splits)};
     ProfScope prof(ctx, st, FFNRM_KERNEL_DOWN);
-    kern<<<grid, ffnrm::kDownWarpsMma * 32, smem, st>>>(p);
+    kern<<<grid, 128, Cfg::smem, st>>>(wmap, ctx->h_map[map_idx][0], ctx->h_map[map_idx][1], p);
     ctx->launches++;
     FFNRM_CUDA(cudaGetLastError());
     return FFNRM_OK;
@@ -418,37 +451,19 @@ int launch_down_t(ffnrm_ctx *ctx, ffnrm::DownMmaParams &p, dim3 grid, cudaStream
 
 int enqueue_down(ffnrm_ctx *ctx, int layer, int T, float *y32, uint16_t *y16, cudaStream_t st) {
     LayerDev &L = ctx->layers[size_t(layer)];
-    const int F = ctx->cfg.d_ff, D = ctx->cfg.d_model;
-    const int F16 = (F + 15) / 16 * 16;
-    ffnrm::DownMmaParams p{};
-    p.h_hi = ctx->h_hi;
-    p.h_lo = ctx->h_lo;
-    p.down_frag = static_cast<const uint4 *>(L.down.ptr);
+    ffnrm::DownUmmaParams p{};
     p.partial = ctx->partial;
     p.tickets = ctx->tickets;
     p.y32 = y32;
     p.y16 = reinterpret_cast<__half *>(y16);
-    p.F16 = F16;
-    p.D = D;
+    p.err = ctx->err;
+    p.D = ctx->cfg.d_model;
+    p.F16 = (ctx->cfg.d_ff + 15) / 16 * 16;
     p.T = T;
-    const int oblocks = D / ffnrm::kDownRowsCta;
-    // ~2 CTAs per SM; slices are multiples of 16 columns of d_ff.
-    int splits = std::max(1, std::min(ctx->max_splits, (2 * ctx->num_sms + oblocks - 1) / oblocks));
-    int kc = (F16 + splits - 1) / splits;
-    kc = (kc + 15) / 16 * 16;
-    splits = (F16 + kc - 1) / kc;
-    p.splits = splits;
-    p.kc = kc;
-    const int NT = T <= 8 ? 1 : (T <= 16 ? 2 : (T <= 32 ? 4 : 8));
-    const dim3 grid{unsigned(oblocks), unsigned(splits), 1u};
-    for (int t0 = 0; t0 < T; t0 += NT * 8) {
-        p.t0 = t0;
-        int rc = NT == 1 ? launch_down_t<1>(ctx, p, grid, st)
-                         : NT == 2 ? launch_down_t<2>(ctx, p, grid, st)
-                                   : NT == 4 ? launch_down_t<4>(ctx, p, grid, st) : launch_down_t<8>(ctx, p, grid, st);
-        if (rc) return rc;
-    }
-    return FFNRM_OK;
+    if (T <= 16) return launch_down_t<16>(ctx, L.down_map, 0, p, st);
+    if (T <= 32) return launch_down_t<32>(ctx, L.down_map, 1, p, st);
+    if (T <= 64) return launch_down_t<64>(ctx, L.down_map, 2, p, st);
+    return launch_down_t<128>(ctx, L.down_map, 3, p, st);
 }
 
 }  // namespace
@@ -480,11 +495,13 @@ int ffnrm_create(ffnrm_ctx **out, int device, const ffnrm_config *cfg) {
     cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
     const size_t TF = size_t(c.max_tokens) * c.d_ff, TD = size_t(c.max_tokens) * c.d_model;
     const size_t F16 = (size_t(c.d_ff) + 15) / 16 * 16;
+    const size_t tickets_bytes = size_t(c.d_model / 128) * ((c.max_tokens + 15) / 16) * sizeof(int);
     const int ntiles = (c.d_ff + c.base_tile_rows - 1) / c.base_tile_rows;
     bool ok = cudaMalloc(&ctx->res[0], TF * 4) == cudaSuccess && cudaMalloc(&ctx->res[1], TF * 4) == cudaSuccess &&
-              cudaMalloc(&ctx->partial, size_t(ctx->max_splits) * 64 * c.d_model * 4) == cudaSuccess &&
-              cudaMalloc(&ctx->tickets, size_t(c.d_model / 256) * sizeof(int)) == cudaSuccess &&
-              cudaMemset(ctx->tickets, 0, size_t(c.d_model / 256) * sizeof(int)) == cudaSuccess &&
+              cudaMalloc(&ctx->partial, ffnrm_ctx::kPartialFloats * 4) == cudaSuccess &&
+              cudaMalloc(&ctx->tickets, tickets_bytes) == cudaSuccess &&
+              cudaMemset(ctx->tickets, 0, tickets_bytes) == cudaSuccess &&
+              cudaMalloc(&ctx->err, sizeof(int)) == cudaSuccess && cudaMemset(ctx->err, 0, sizeof(int)) == cudaSuccess &&
               cudaMalloc(&ctx->h_hi, size_t(c.max_tokens) * F16 * 2) == cudaSuccess &&
               cudaMalloc(&ctx->h_lo, size_t(c.max_tokens) * F16 * 2) == cudaSuccess &&
               cudaMalloc(&ctx->y16_dev, TD * 2) == cudaSuccess;
@@ -503,6 +520,13 @@ int ffnrm_create(ffnrm_ctx **out, int device, const ffnrm_config *cfg) {
         ffnrm_destroy(ctx);
         return fail(FFNRM_ERR_NOMEM, "workspace allocation failed (max_tokens=%d, d_ff=%d)", c.max_tokens, c.d_ff);
     }
+    const uint32_t tiles[4] = {16, 32, 64, 128};
+    for (int i = 0; i < 4; ++i)
+        if (!make_fp16_map(&ctx->h_map[i][0], ctx->h_hi, F16, size_t(c.max_tokens), F16, tiles[i]) ||
+            !make_fp16_map(&ctx->h_map[i][1], ctx->h_lo, F16, size_t(c.max_tokens), F16, tiles[i])) {
+            ffnrm_destroy(ctx);
+            return fail(FFNRM_ERR_CUDA, "cuTensorMapEncodeTiled unavailable or rejected the h buffers");
+        }
     *out = ctx;
     return FFNRM_OK;
 }
@@ -516,6 +540,7 @@ int ffnrm_destroy(ffnrm_ctx *ctx) {
     cudaFree(ctx->res[1]);
     cudaFree(ctx->partial);
     cudaFree(ctx->tickets);
+    cudaFree(ctx->err);
     cudaFree(ctx->h_hi);
     cudaFree(ctx->h_lo);
     cudaFree(ctx->y16_dev);
@@ -578,6 +603,9 @@ int ffnrm_load_layer(ffnrm_ctx *ctx, int layer, const ffnrm_layer_weights *w) {
         rc = upload_scales(L.alpha[q], alpha[q], F, G, L.scales_half);
     }
     if (rc == FFNRM_OK) rc = upload_down(L.down, w->down, w->down_ld, F, D);
+    if (rc == FFNRM_OK && !make_fp16_map(&L.down_map, L.down.ptr, uint64_t((F + 15) / 16 * 16), uint64_t(D),
+                                         uint64_t((F + 15) / 16 * 16), 128))
+        rc = fail(FFNRM_ERR_CUDA, "cuTensorMapEncodeTiled rejected the down weight");
     if (rc) {
         free_layer(L);
         return rc;
@@ -696,6 +724,21 @@ int ffnrm_layer_bytes(ffnrm_ctx *ctx, int layer, int64_t *residual_bytes, int64_
 }
 
 int64_t ffnrm_launch_count(ffnrm_ctx *ctx) { return ctx ? ctx->launches : -1; }
+
+int ffnrm_check_device_error(ffnrm_ctx *ctx, void *stream) {
+    if (!ctx) return fail(FFNRM_ERR_ARG, "null context");
+    DeviceGuard guard(ctx->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int code = 0;
+    FFNRM_CUDA(cudaMemcpyAsync(&code, ctx->err, sizeof(int), cudaMemcpyDeviceToHost, st));
+    FFNRM_CUDA(cudaStreamSynchronize(st));
+    if (code) {
+        FFNRM_CUDA(cudaMemsetAsync(ctx->err, 0, sizeof(int), st));
+        FFNRM_CUDA(cudaStreamSynchronize(st));
+        return fail(FFNRM_ERR_TIMEOUT, "a kernel gave up waiting on a pipeline barrier (code %d)", code);
+    }
+    return FFNRM_OK;
+}
 
 int ffnrm_profile_enable(ffnrm_ctx *ctx, int enable) {
     if (!ctx) return fail(FFNRM_ERR_ARG, "null context");

@@ -84,4 +84,9 @@ __device__ __forceinline__ int dot_plane(uint32_t w, const uint4 &z0, const uint
     return a;
 }
 
+__global__ void cast_f16_kernel(const float *src, __half *dst, int64_t n) {
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
+        dst[i] = __float2half_rn(src[i]);
+}
+
 }  // namespace ffnrm

@@ -149,6 +149,10 @@ class ResidualMesh:
     def launches(self) -> int:
         return int(self.lib.ffnrm_launch_count(self.handle))
 
+    def check_device_error(self, stream=None) -> None:
+        """Synchronise and raise TimeoutError if a kernel gave up on a bounded wait."""
+        N.check(self.lib.ffnrm_check_device_error(self.handle, _stream(stream)))
+
     def profile(self, enable: bool) -> None:
         """Start (and clear) or stop live per-kernel CUDA-event timing."""
         N.check(self.lib.ffnrm_profile_enable(self.handle, int(enable)))

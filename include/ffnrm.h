@@ -41,6 +41,7 @@ extern "C" {
 #define FFNRM_ERR_CUDA 2    /* CUDA runtime error */
 #define FFNRM_ERR_STATE 3   /* e.g. layer not loaded, fallback data missing */
 #define FFNRM_ERR_NOMEM 4   /* device or pinned allocation failed */
+#define FFNRM_ERR_TIMEOUT 5 /* a kernel's bounded pipeline wait expired (reported by ffnrm_check_device_error) */
 
 /* Residual code formats accepted by ffnrm_load_layer. */
 #define FFNRM_CODES_Q4_BYTES 0       /* full Q4 codes, one byte per code [F, D], values 0..15 */
@@ -139,6 +140,10 @@ int ffnrm_cast_f16(const float *src, uint16_t *dst, int64_t n, void *stream);
 
 /* Device bytes held by loaded weights / workspace (for the bench's byte accounting). */
 int ffnrm_layer_bytes(ffnrm_ctx *ctx, int layer, int64_t *residual_bytes, int64_t *down_bytes);
+
+/* Synchronises `stream` and reports whether any kernel of this context gave up on a
+ * bounded pipeline wait since the last check (FFNRM_ERR_TIMEOUT, error word cleared). */
+int ffnrm_check_device_error(ffnrm_ctx *ctx, void *stream);
 
 /* Kernel launches issued by this context since creation (the bench's launch count). */
 int64_t ffnrm_launch_count(ffnrm_ctx *ctx);
