@@ -51,6 +51,7 @@ def parse():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", default="c2", choices=("c2",))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--eager", action="store_true", help="time eager calls instead of CUDA-graph replays")
     ap.add_argument("--layers", type=int, default=None, help="override the stack depth (profiling cases)")
     ap.add_argument("--tokens", type=str, default=None, help="override the decode batches, e.g. 64 or 1,8")
     return ap.parse_args()
@@ -177,6 +178,7 @@ def run_ours(args, cfg, rank, world, local_rank):
     import torch.distributed as dist
 
     from ffn_residual_mesh_b200.engine import LayerSpec
+    from ffn_residual_mesh_b200.graphs import StepGraph
     from ffn_residual_mesh_b200.shard import ShardedFfnStack
 
     dev = torch.device("cuda", local_rank)
@@ -224,15 +226,12 @@ def run_ours(args, cfg, rank, world, local_rank):
                 h = inputs[(T, l)]["host"]
                 stack.forward_host(l, h["z"], h["s"], h["gb"], h["ub"], h["y16"], staging=staging)
 
-    def timed(fn, steps, profile=False):
+    def timed(fn, steps):
         for _ in range(args.warmup):
             fn()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-        if profile:
-            mesh.profile(True)
-        launches0 = mesh.launches
         start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record()
         for _ in range(steps):
@@ -240,24 +239,53 @@ def run_ours(args, cfg, rank, world, local_rank):
         stop.record()
         torch.cuda.synchronize()
         ms = start.elapsed_time(stop)
-        prof = mesh.profile_read() if profile else None
-        if profile:
-            mesh.profile(False)
-        launches = mesh.launches - launches0
         if world > 1:
             t = torch.tensor([ms], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ms = float(t.item())
             dist.barrier()
-        return ms, launches, prof
+        return ms
+
+    use_graphs = world == 1 and not args.eager
+    launches0 = mesh.launches
+    step_device()
+    torch.cuda.synchronize()
+    launches_per_step = mesh.launches - launches0
+    if use_graphs:
+        g_dev, g_e2e = StepGraph(step_device), StepGraph(step_e2e)
+        run_dev, run_e2e = g_dev.replay, g_e2e.replay
+    else:
+        run_dev, run_e2e = step_device, step_e2e
 
     clocks = ClockSampler(local_rank)
     clocks.start()
-    dev_ms, launches, prof = timed(step_device, args.steps, profile=True)
+    dev_ms = timed(run_dev, args.steps)
     clock_info = clocks.stop()
-    e2e_ms, _, _ = timed(step_e2e, args.steps)
-    # unprofiled device timing (profiling events add host work between launches)
-    dev_ms_plain, _, _ = timed(step_device, args.steps)
+    e2e_ms = timed(run_e2e, args.steps)
+    eager_ms = timed(step_device, args.steps) if use_graphs else dev_ms
+    eager_e2e_ms = timed(step_e2e, args.steps) if use_graphs else e2e_ms
+
+    # Per-kernel device time over K steps: CUDA events recorded around each launch on the
+    # launching stream (captured as graph nodes when graphs are used).
+    mesh.profile(True)
+    prof = {"residual": [0.0, 0], "down": [0.0, 0]}
+    if use_graphs:
+        g_prof = StepGraph(step_device, warmup=0)
+        for _ in range(args.steps):
+            g_prof.replay()
+            for k, (ms, n) in mesh.profile_read().items():
+                if k in prof:
+                    prof[k][0] += ms
+                    prof[k][1] += n
+        g_prof.close()
+    else:
+        for _ in range(args.steps):
+            step_device()
+        for k, (ms, n) in mesh.profile_read().items():
+            if k in prof:
+                prof[k] = [ms, n]
+    mesh.profile(False)
+    launches = launches_per_step * args.steps
 
     per_batch = {}
     for T in cfg.tokens:
@@ -265,29 +293,37 @@ def run_ours(args, cfg, rank, world, local_rank):
             for l in range(cfg.layers):
                 b = inputs[(T, l)]
                 stack.forward(l, b["z"], b["s"], b["gb"], b["ub"], b["y16"])
-        ms_b, _, prof_b = timed(one_batch, args.steps, profile=True)
+        runner = StepGraph(one_batch) if use_graphs else None
+        ms_b = timed(runner.replay if runner else one_batch, args.steps)
         per_batch[str(T)] = {"ms_per_stack": ms_b / args.steps, "tokens_per_s": T * args.steps / (ms_b / 1e3),
-                             "us_per_layer": {k: 1e3 * v[0] / max(v[1], 1) for k, v in prof_b.items() if v[1]}}
+                             "us_per_layer": 1e3 * ms_b / args.steps / cfg.layers}
+        if runner:
+            runner.close()
+    if use_graphs:
+        g_dev.close()
+        g_e2e.close()
+    mesh.check_device_error()
 
     tokens_step = sum(cfg.tokens)
-    value = tokens_step * args.steps / (dev_ms_plain / 1e3)
+    value = tokens_step * args.steps / (dev_ms / 1e3)
     e2e_value = tokens_step * args.steps / (e2e_ms / 1e3)
 
     # roofline: algorithmic bytes per launch / live CUDA-event time per launch
     res_bytes_layer, down_bytes_layer = mesh.layer_bytes(0)
     D, G = cfg.d_model, cfg.d_model // 32
-    alg = {"residual": 0, "down": 0, "reduce": 0}
+    alg = {"residual": 0, "down": 0}
     for T in cfg.tokens:
-        alg["residual"] += cfg.layers * (res_bytes_layer + T * D + T * G * 4 + 2 * T * F * 4)
-        # down: fp16 weights + residual and base in + split-K partials out (upper bound: 16 splits)
-        alg["down"] += cfg.layers * (down_bytes_layer + 4 * T * F * 4)
-        alg["reduce"] += cfg.layers * (T * D * 2)
+        # codes + alpha, activations and scales, both base sums in, h (fp16 hi + lo) out
+        alg["residual"] += cfg.layers * (res_bytes_layer + T * D + T * G * 4 + 2 * T * F * 4 + T * F * 4)
+        # fp16 down weight, h (hi + lo) in, y (fp16) out
+        alg["down"] += cfg.layers * (down_bytes_layer + T * F * 4 + T * D * 2)
     alg = {k: v * args.steps for k, v in alg.items()}
     peak, peak_kind = peaks()
     kern = {}
     for k, (ms, n) in prof.items():
         if n:
-            kern[k] = {"ms_total": ms, "launches": n, "achieved_gbs": alg[k] / (ms / 1e3) / 1e9 if ms else None}
+            kern[k] = {"ms_total": ms, "launches": n, "achieved_gbs": alg[k] / (ms / 1e3) / 1e9 if ms else None,
+                       "us_per_launch": 1e3 * ms / n}
     dom = max(kern, key=lambda k: kern[k]["ms_total"])
     traffic = None
     tfile = ROOT / "profiles" / "traffic.json"
@@ -304,6 +340,7 @@ def run_ours(args, cfg, rank, world, local_rank):
                            "frac": kern["residual"]["achieved_gbs"] / peak,
                            "ms_per_launch": kern["residual"]["ms_total"] / kern["residual"]["launches"]}
 
+
     h2d = sum(cfg.layers * (T * D + T * G * 4 + 2 * T * F * 4) for T in cfg.tokens)
     d2h = sum(cfg.layers * T * D * 2 for T in cfg.tokens)
     cpu = None
@@ -319,12 +356,16 @@ def run_ours(args, cfg, rank, world, local_rank):
     if rank == 0:
         print(json.dumps({
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": dev_ms_plain / args.steps, "higher_is_better": True,
+            "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None,
             "dtype": "int8 x u2 -> int32 residual, fp16 x fp32 down", "data": "synthetic",
             "config": config_block(cfg, world),
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d * world,
-                    "d2h_bytes_per_step": d2h * world, "ms_per_step": e2e_ms / args.steps},
+                    "d2h_bytes_per_step": d2h * world, "ms_per_step": e2e_ms / args.steps,
+                    "path": "ShardedFfnStack.forward_host -> ffnrm_ffn_forward_host"
+                            + (" (CUDA graph replay)" if use_graphs else ""),
+                    "eager_value": tokens_step * args.steps / (eager_e2e_ms / 1e3)},
+            "eager_value": tokens_step * args.steps / (eager_ms / 1e3), "cuda_graphs": use_graphs,
             "roofline": roofline, "residual_kernel": residual_kernel, "kernels": kern, "per_batch": per_batch,
             "cpu_baseline": cpu, "gpu_launches": launches, "clocks": clock_info,
             "setup_s": round(setup_s, 1),

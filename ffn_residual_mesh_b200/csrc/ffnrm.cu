@@ -113,6 +113,8 @@ struct ffnrm_ctx {
     cudaStream_t copy_stream = nullptr;
     cudaEvent_t base_ready[2] = {nullptr, nullptr}, slot_free[2] = {nullptr, nullptr};
     int slot = 0;
+    unsigned long long capture_id = 0;  // stream capture the slot events below belong to
+    bool slot_in_capture[2] = {false, false};
     int64_t launches = 0;
     int num_sms = 148;
     // live profiling: event pairs around launches, resolved by ffnrm_profile_read
@@ -120,8 +122,6 @@ struct ffnrm_ctx {
     std::vector<cudaEvent_t> prof_pool;
     size_t prof_used = 0;
     std::vector<int> prof_kind;
-    double prof_ms[3] = {0, 0, 0};
-    int64_t prof_count[3] = {0, 0, 0};
 };
 
 namespace {
@@ -663,6 +663,21 @@ int ffnrm_ffn_forward_host(ffnrm_ctx *ctx, int layer, const int8_t *z, const flo
     ctx->slot ^= 1;
     const size_t tf_bytes = size_t(tokens) * F * 4;
     cudaStream_t cs = ctx->copy_stream;
+    // Inside a CUDA graph capture the copy stream may only wait on events recorded in the
+    // same capture: the first use of each slot in a capture forks from `stream` here.
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    unsigned long long cap_id = 0;
+    FFNRM_CUDA(cudaStreamGetCaptureInfo(st, &cap, &cap_id));
+    if (cap == cudaStreamCaptureStatusActive) {
+        if (cap_id != ctx->capture_id) {
+            ctx->capture_id = cap_id;
+            ctx->slot_in_capture[0] = ctx->slot_in_capture[1] = false;
+        }
+        if (!ctx->slot_in_capture[sl]) {
+            FFNRM_CUDA(cudaEventRecord(ctx->slot_free[sl], st));
+            ctx->slot_in_capture[sl] = true;
+        }
+    }
     // Every upload goes on the copy stream into slot `sl`, which the call before the
     // previous one has released; the next layer's upload thus overlaps this layer's kernels.
     FFNRM_CUDA(cudaStreamWaitEvent(cs, ctx->slot_free[sl], 0));
@@ -747,25 +762,27 @@ int ffnrm_profile_enable(ffnrm_ctx *ctx, int enable) {
     ctx->prof = enable != 0;
     ctx->prof_used = 0;
     ctx->prof_kind.clear();
-    for (int k = 0; k < 3; ++k) ctx->prof_ms[k] = 0, ctx->prof_count[k] = 0;
     return FFNRM_OK;
 }
 
+// Sums the device time of the recorded launch pairs of `kind`. The records stay, so a
+// CUDA graph captured with profiling on can be replayed and read again after each replay.
 int ffnrm_profile_read(ffnrm_ctx *ctx, int kind, double *total_ms, int64_t *launches) {
     if (!ctx || kind < 0 || kind > 2) return fail(FFNRM_ERR_ARG, "bad profile arguments");
     DeviceGuard guard(ctx->device);
+    double ms_sum = 0;
+    int64_t n = 0;
     for (size_t i = 0; i < ctx->prof_kind.size(); ++i) {
+        if (ctx->prof_kind[i] != kind) continue;
         cudaEvent_t a = ctx->prof_pool[2 * i], b = ctx->prof_pool[2 * i + 1];
         FFNRM_CUDA(cudaEventSynchronize(b));
         float ms = 0.f;
         FFNRM_CUDA(cudaEventElapsedTime(&ms, a, b));
-        ctx->prof_ms[ctx->prof_kind[i]] += ms;
-        ctx->prof_count[ctx->prof_kind[i]] += 1;
+        ms_sum += ms;
+        ++n;
     }
-    ctx->prof_kind.clear();
-    ctx->prof_used = 0;
-    if (total_ms) *total_ms = ctx->prof_ms[kind];
-    if (launches) *launches = ctx->prof_count[kind];
+    if (total_ms) *total_ms = ms_sum;
+    if (launches) *launches = n;
     return FFNRM_OK;
 }
 

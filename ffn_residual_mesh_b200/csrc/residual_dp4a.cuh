@@ -110,47 +110,67 @@ __global__ void __launch_bounds__(2 * kResWarps * 32) residual_gemv_kernel(const
 #pragma unroll
     for (int t = 0; t < TT; ++t) acc[t] = 0.f;
 
-#pragma unroll 2
-    for (int c = c_begin; c < c_end; ++c) {
-        const int64_t rec = (int64_t(rb) * C + c) * 32 + lane;
-        uint4 wp = make_uint4(0, 0, 0, 0), wh = wp;
-        uint2 wq = make_uint2(0, 0);
-        if (RB != 1 || flagged) wp = __ldg(pv.pair + rec);
-        if (RB != 2) wq = __ldg(pv.plane + rec);
-        float a0, a1, b0 = 0.f, b1 = 0.f;
-        load_scale2<AHALF>(pv.alpha, rec, a0, a1);
-        if (flagged) {
-            wh = __ldg(pv.pair_hi + rec);
-            load_scale2<AHALF>(pv.beta, rec, b0, b1);
-        }
+    // Loads of kBatch chunks are issued together before any is used, keeping
+    // kBatch x 20 bytes per lane in flight.
+    constexpr int kBatch = 8;
+    for (int cb = c_begin; cb < c_end; cb += kBatch) {
+        uint4 wpb[kBatch], whb[kBatch];
+        uint2 wqb[kBatch];
+        float a0b[kBatch], a1b[kBatch], b0b[kBatch], b1b[kBatch];
 #pragma unroll
-        for (int t = 0; t < TT; ++t) {
-            const uint4 *zv = reinterpret_cast<const uint4 *>(z_sm + t * D + c * 64);
-            const uint4 z0 = zv[0], z1 = zv[1], z2 = zv[2], z3 = zv[3];
-            int P0, P1;
-            if (RB == 1) {
-                P0 = dot_plane(wq.x, z0, z1);
-                P1 = dot_plane(wq.y, z2, z3);
-            } else {
-                P0 = dot_pair(wp.x, wp.y, z0, z1);
-                P1 = dot_pair(wp.z, wp.w, z2, z3);
-                if (RB == 3) {
-                    P0 += 4 * dot_plane(wq.x, z0, z1);
-                    P1 += 4 * dot_plane(wq.y, z2, z3);
+        for (int u = 0; u < kBatch; ++u) {
+            const int c = cb + u;
+            wpb[u] = make_uint4(0, 0, 0, 0);
+            whb[u] = wpb[u];
+            wqb[u] = make_uint2(0, 0);
+            a0b[u] = a1b[u] = b0b[u] = b1b[u] = 0.f;
+            if (c < c_end) {
+                const int64_t rec = (int64_t(rb) * C + c) * 32 + lane;
+                if (RB != 1 || flagged) wpb[u] = __ldg(pv.pair + rec);
+                if (RB != 2) wqb[u] = __ldg(pv.plane + rec);
+                load_scale2<AHALF>(pv.alpha, rec, a0b[u], a1b[u]);
+                if (flagged) {
+                    whb[u] = __ldg(pv.pair_hi + rec);
+                    load_scale2<AHALF>(pv.beta, rec, b0b[u], b1b[u]);
                 }
             }
-            const float s0 = s_sm[t * G + 2 * c], s1 = s_sm[t * G + 2 * c + 1];
-            if (p.dots != nullptr && valid && t0 + t < T)
-                *reinterpret_cast<int2 *>(p.dots + ((int64_t(proj) * T + t0 + t) * F + row) * G + 2 * c) =
-                    make_int2(P0, P1);
-            if (flagged) {
-                const int F0 = dot_pair(wp.x, wp.y, z0, z1) + 4 * dot_pair(wh.x, wh.y, z0, z1);
-                const int F1 = dot_pair(wp.z, wp.w, z2, z3) + 4 * dot_pair(wh.z, wh.w, z2, z3);
-                const float zs0 = zsum_sm[t * G + 2 * c], zs1 = zsum_sm[t * G + 2 * c + 1];
-                acc[t] += s0 * (a0 * float(F0) + b0 * zs0) + s1 * (a1 * float(F1) + b1 * zs1);
-            } else {
-                acc[t] = fmaf(float(P0), a0 * s0, acc[t]);
-                acc[t] = fmaf(float(P1), a1 * s1, acc[t]);
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const int c = cb + u;
+            if (c >= c_end) break;
+            const uint4 wp = wpb[u], wh = whb[u];
+            const uint2 wq = wqb[u];
+            const float a0 = a0b[u], a1 = a1b[u], b0 = b0b[u], b1 = b1b[u];
+#pragma unroll
+            for (int t = 0; t < TT; ++t) {
+                const uint4 *zv = reinterpret_cast<const uint4 *>(z_sm + t * D + c * 64);
+                const uint4 z0 = zv[0], z1 = zv[1], z2 = zv[2], z3 = zv[3];
+                int P0, P1;
+                if (RB == 1) {
+                    P0 = dot_plane(wq.x, z0, z1);
+                    P1 = dot_plane(wq.y, z2, z3);
+                } else {
+                    P0 = dot_pair(wp.x, wp.y, z0, z1);
+                    P1 = dot_pair(wp.z, wp.w, z2, z3);
+                    if (RB == 3) {
+                        P0 += 4 * dot_plane(wq.x, z0, z1);
+                        P1 += 4 * dot_plane(wq.y, z2, z3);
+                    }
+                }
+                const float s0 = s_sm[t * G + 2 * c], s1 = s_sm[t * G + 2 * c + 1];
+                if (p.dots != nullptr && valid && t0 + t < T)
+                    *reinterpret_cast<int2 *>(p.dots + ((int64_t(proj) * T + t0 + t) * F + row) * G + 2 * c) =
+                        make_int2(P0, P1);
+                if (flagged) {
+                    const int F0 = dot_pair(wp.x, wp.y, z0, z1) + 4 * dot_pair(wh.x, wh.y, z0, z1);
+                    const int F1 = dot_pair(wp.z, wp.w, z2, z3) + 4 * dot_pair(wh.z, wh.w, z2, z3);
+                    const float zs0 = zsum_sm[t * G + 2 * c], zs1 = zsum_sm[t * G + 2 * c + 1];
+                    acc[t] += s0 * (a0 * float(F0) + b0 * zs0) + s1 * (a1 * float(F1) + b1 * zs1);
+                } else {
+                    acc[t] = fmaf(float(P0), a0 * s0, acc[t]);
+                    acc[t] = fmaf(float(P1), a1 * s1, acc[t]);
+                }
             }
         }
     }

@@ -150,9 +150,10 @@ int64_t ffnrm_launch_count(ffnrm_ctx *ctx);
 
 /* Live per-kernel timing with CUDA events recorded on the launching stream around
  * each of this context's kernel launches (off by default; enabling clears the
- * totals). Kinds: FFNRM_KERNEL_RESIDUAL, FFNRM_KERNEL_DOWN, FFNRM_KERNEL_REDUCE.
+ * records). Kinds: FFNRM_KERNEL_RESIDUAL, FFNRM_KERNEL_DOWN, FFNRM_KERNEL_REDUCE.
  * ffnrm_profile_read waits for the recorded events and returns the summed device
- * time and the launch count of that kind since enabling. */
+ * time and launch count of that kind over the records; records are kept, so calls
+ * captured into a CUDA graph with profiling on can be read after every replay. */
 #define FFNRM_KERNEL_RESIDUAL 0
 #define FFNRM_KERNEL_DOWN 1
 #define FFNRM_KERNEL_REDUCE 2

@@ -285,3 +285,39 @@ def test_empty_batch_is_a_no_op(cuda):
     ctx.forward(0, z, s, e, e, y32=torch.empty(0, D, device=cuda))
     torch.cuda.synchronize()
     ctx.close()
+
+
+def test_graph_capture_of_host_streamed_calls(cuda):
+    """A captured sequence of host-streamed forwards (copy-stream fork/join inside the
+    capture) replays to the same output; host buffers refilled in place are picked up."""
+    import torch
+    from ffn_residual_mesh_b200.graphs import StepGraph
+    c = load("c2_decode_t8_r2")
+    F, D, T = int(c["F"]), int(c["D"]), int(c["T"])
+    ctx = make_ctx(c)
+    pin = lambda a: torch.from_numpy(np.ascontiguousarray(a)).pin_memory()
+    z, s = pin(c["z"]), pin(c["s"])
+    gb, ub = pin(c["host"].astype(np.float32)), pin(c["host_up"].astype(np.float32))
+    ys = [torch.zeros(T, D, dtype=torch.float16).pin_memory() for _ in range(3)]
+
+    def step():
+        for y in ys:
+            ctx.forward_host(0, z, s, gb, ub, y)
+
+    g = StepGraph(step)
+    for y in ys:
+        y.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    for y in ys:
+        assert rel_l2(y.float().numpy(), c["y"]) < Y_REL_L2
+    gb.zero_()   # a changed host input is read by the next replay
+    ub.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    ref0 = O.ffn_forward(c["codes"], c["codes_up"], c["alpha"], c["alpha_up"], c["beta"], c["beta_up"], c["down"],
+                         c["z"], c["s"], int(c["r"]), gate_base=np.zeros((T, F)), up_base=np.zeros((T, F)))["y"]
+    assert rel_l2(ys[0].float().numpy(), ref0) < Y_REL_L2
+    ctx.check_device_error()
+    g.close()
+    ctx.close()
