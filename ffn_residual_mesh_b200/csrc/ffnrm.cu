@@ -677,6 +677,12 @@ int ffnrm_ffn_forward_host(ffnrm_ctx *ctx, int layer, const int8_t *z, const flo
             FFNRM_CUDA(cudaEventRecord(ctx->slot_free[sl], st));
             ctx->slot_in_capture[sl] = true;
         }
+    } else if (ctx->capture_id != 0) {
+        // The slot events were last recorded as nodes of a capture, which an eager wait
+        // may not reference: record them again on `stream`.
+        for (int i = 0; i < 2; ++i) FFNRM_CUDA(cudaEventRecord(ctx->slot_free[i], st));
+        ctx->capture_id = 0;
+        ctx->slot_in_capture[0] = ctx->slot_in_capture[1] = false;
     }
     // Every upload goes on the copy stream into slot `sl`, which the call before the
     // previous one has released; the next layer's upload thus overlaps this layer's kernels.

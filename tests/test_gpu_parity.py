@@ -321,3 +321,27 @@ def test_graph_capture_of_host_streamed_calls(cuda):
     ctx.check_device_error()
     g.close()
     ctx.close()
+
+
+def test_eager_call_after_capture(cuda):
+    """Eager host-streamed calls keep working after a captured sequence."""
+    import torch
+    from ffn_residual_mesh_b200.graphs import StepGraph
+    c = load("c2_decode_t8_r2")
+    T, D = int(c["T"]), int(c["D"])
+    ctx = make_ctx(c)
+    pin = lambda a: torch.from_numpy(np.ascontiguousarray(a)).pin_memory()
+    z, s = pin(c["z"]), pin(c["s"])
+    gb, ub = pin(c["host"].astype(np.float32)), pin(c["host_up"].astype(np.float32))
+    y = torch.zeros(T, D, dtype=torch.float16).pin_memory()
+    g = StepGraph(lambda: ctx.forward_host(0, z, s, gb, ub, y))
+    g.replay()
+    for _ in range(3):
+        y.zero_()
+        ctx.forward_host(0, z, s, gb, ub, y)
+        torch.cuda.synchronize()
+        assert rel_l2(y.float().numpy(), c["y"]) < Y_REL_L2
+    g.replay()
+    torch.cuda.synchronize()
+    g.close()
+    ctx.close()
