@@ -320,18 +320,28 @@ struct ProfScope {
     cudaStream_t st;
     int kind;
     bool on;
+    // Inside a stream capture the events become external event-record nodes of the graph,
+    // so they can be read after each replay.
+    static void record(cudaEvent_t e, cudaStream_t st) {
+        cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+        cudaStreamIsCapturing(st, &cap);
+        if (cap == cudaStreamCaptureStatusActive)
+            cudaEventRecordWithFlags(e, st, cudaEventRecordExternal);
+        else
+            cudaEventRecord(e, st);
+    }
     ProfScope(ffnrm_ctx *c, cudaStream_t s, int k) : ctx(c), st(s), kind(k), on(c->prof) {
         if (on) {
             cudaEvent_t e = prof_event(ctx);
             if (!e) { on = false; return; }
-            cudaEventRecord(e, st);
+            record(e, st);
         }
     }
     ~ProfScope() {
         if (!on) return;
         cudaEvent_t e = prof_event(ctx);
         if (!e) { ctx->prof_used--; return; }
-        cudaEventRecord(e, st);
+        record(e, st);
         ctx->prof_kind.push_back(kind);
     }
 };
