@@ -33,6 +33,8 @@ SIGNATURES = {
     "ffnrm_layer_bytes": (c_int, [c_void_p, c_int, POINTER(c_int64), POINTER(c_int64)]),
     "ffnrm_launch_count": (c_int64, [c_void_p]),
     "ffnrm_check_device_error": (c_int, [c_void_p, c_void_p]),
+    "ffnrm_down_project_noalloc": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int, c_int, c_int,
+                                           c_void_p, c_void_p, c_void_p, c_void_p]),
     "ffnrm_profile_enable": (c_int, [c_void_p, c_int]),
     "ffnrm_profile_read": (c_int, [c_void_p, c_int, POINTER(ctypes.c_double), POINTER(c_int64)]),
     "ffnrm_last_error": (c_char_p, []),

@@ -14,6 +14,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <new>
 #include <string>
 #include <vector>
@@ -476,6 +477,85 @@ int enqueue_down(ffnrm_ctx *ctx, int layer, int T, float *y32, uint16_t *y16, cu
     return launch_down_t<128>(ctx, L.down_map, 3, p, st);
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free down projection: scratch in file-scope device arrays
+// ---------------------------------------------------------------------------
+constexpr size_t kNoAllocPartialFloats = size_t(1) << 21;  // split-K partials: 8 MiB per device
+constexpr int kNoAllocTickets = 2048;                      // (d_model/128) x token tiles
+constexpr int kNoAllocMaxTokens = 256;
+constexpr int kNoAllocMaxDModel = 16384;
+constexpr int kNoAllocMaxDevices = 64;
+
+// Held by every GPU that loads this library, until the process exits.
+__device__ __align__(256) float g_noalloc_partial[kNoAllocPartialFloats];
+__device__ __align__(256) int g_noalloc_tickets[kNoAllocTickets];
+__device__ __align__(256) int g_noalloc_status[64];
+
+struct NoAllocScratch {
+    float *partial = nullptr;
+    int *tickets = nullptr;
+    int *status = nullptr;
+};
+std::mutex g_noalloc_mutex;
+NoAllocScratch g_noalloc[kNoAllocMaxDevices];
+
+// Device addresses of the scratch arrays on `dev` (the current device), looked up once.
+int noalloc_scratch(int dev, NoAllocScratch &out) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    NoAllocScratch &s = g_noalloc[dev];
+    if (!s.partial) {
+        NoAllocScratch t;
+        FFNRM_CUDA(cudaGetSymbolAddress(reinterpret_cast<void **>(&t.partial), g_noalloc_partial));
+        FFNRM_CUDA(cudaGetSymbolAddress(reinterpret_cast<void **>(&t.tickets), g_noalloc_tickets));
+        FFNRM_CUDA(cudaGetSymbolAddress(reinterpret_cast<void **>(&t.status), g_noalloc_status));
+        s = t;
+    }
+    out = s;
+    return FFNRM_OK;
+}
+
+template <int N>
+int launch_down_noalloc(const uint16_t *down, int64_t down_ld, const uint16_t *h_hi, const uint16_t *h_lo,
+                        int64_t h_ld, int D, int F, int T, float *y32, uint16_t *y16, int32_t *status,
+                        const NoAllocScratch &scr, cudaStream_t st) {
+    using Cfg = ffnrm::DownUmmaCfg<N>;
+    CUtensorMap wm, hm, lm;
+    if (!make_fp16_map(&wm, down, uint64_t(F), uint64_t(D), uint64_t(down_ld), 128) ||
+        !make_fp16_map(&hm, h_hi, uint64_t(F), uint64_t(T), uint64_t(h_ld), N) ||
+        !make_fp16_map(&lm, h_lo, uint64_t(F), uint64_t(T), uint64_t(h_ld), N))
+        return fail(FFNRM_ERR_CUDA, "cuTensorMapEncodeTiled rejected the down weight or h");
+    auto kern = ffnrm::down_umma_kernel<N>;
+    FFNRM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::smem)));
+    int dev = 0, sms = 148;
+    FFNRM_CUDA(cudaGetDevice(&dev));
+    FFNRM_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int occ = Cfg::smem <= 113 * 1024 ? 2 : 1;
+    const int mt = D / ffnrm::kUmmaM, ntile = (T + N - 1) / N;
+    const int F16 = (F + 15) / 16 * 16;
+    const int ksteps = (F16 + ffnrm::kUmmaK - 1) / ffnrm::kUmmaK;
+    int splits = std::max(1, std::min(ksteps, occ * sms / (mt * ntile)));
+    while (splits > 1 && size_t(splits) * T * D > kNoAllocPartialFloats) --splits;
+    const int kc_steps = (ksteps + splits - 1) / splits;
+    splits = (ksteps + kc_steps - 1) / kc_steps;
+    ffnrm::DownUmmaParams p{};
+    p.partial = scr.partial;
+    p.tickets = scr.tickets;
+    p.y32 = y32;
+    p.y16 = reinterpret_cast<__half *>(y16);
+    p.err = status ? status : scr.status;
+    p.D = D;
+    p.F16 = F16;
+    p.T = T;
+    p.splits = splits;
+    p.kc = kc_steps * ffnrm::kUmmaK;
+    // The arrays keep the previous call's contents: tickets and status must start at zero.
+    FFNRM_CUDA(cudaMemsetAsync(scr.tickets, 0, size_t(mt) * ntile * sizeof(int), st));
+    FFNRM_CUDA(cudaMemsetAsync(p.err, 0, sizeof(int), st));
+    kern<<<dim3(unsigned(mt), unsigned(ntile), unsigned(splits)), 128, Cfg::smem, st>>>(wm, hm, lm, p);
+    FFNRM_CUDA(cudaGetLastError());
+    return FFNRM_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -755,6 +835,36 @@ int ffnrm_layer_bytes(ffnrm_ctx *ctx, int layer, int64_t *residual_bytes, int64_
 }
 
 int64_t ffnrm_launch_count(ffnrm_ctx *ctx) { return ctx ? ctx->launches : -1; }
+
+int ffnrm_down_project_noalloc(const uint16_t *down, int64_t down_ld, const uint16_t *h_hi, const uint16_t *h_lo,
+                               int64_t h_ld, int d_model, int d_ff, int tokens, float *y_f32, uint16_t *y_f16,
+                               int32_t *status, void *stream) {
+    if (tokens < 0 || tokens > kNoAllocMaxTokens)
+        return fail(FFNRM_ERR_ARG, "tokens=%d outside [0, %d] (the scratch of the allocation-free call is fixed)",
+                    tokens, kNoAllocMaxTokens);
+    if (d_model <= 0 || d_model % 128 || d_model > kNoAllocMaxDModel)
+        return fail(FFNRM_ERR_ARG, "d_model=%d must be a positive multiple of 128 up to %d", d_model,
+                    kNoAllocMaxDModel);
+    if (d_ff <= 0) return fail(FFNRM_ERR_ARG, "d_ff=%d must be positive", d_ff);
+    if (!down || !h_hi || !h_lo || (!y_f32 && !y_f16)) return fail(FFNRM_ERR_ARG, "null device pointer");
+    if (down_ld < d_ff || h_ld < d_ff || down_ld % 8 || h_ld % 8)
+        return fail(FFNRM_ERR_ARG, "down_ld and h_ld must be >= d_ff and multiples of 8");
+    if (!aligned(down, 16) || !aligned(h_hi, 16) || !aligned(h_lo, 16) || !aligned(y_f32, 4) || !aligned(y_f16, 2) ||
+        !aligned(status, 4))
+        return fail(FFNRM_ERR_ARG, "down, h_hi and h_lo must be 16-byte aligned");
+    if (tokens == 0) return FFNRM_OK;
+    int dev = 0;
+    FFNRM_CUDA(cudaGetDevice(&dev));
+    if (dev >= kNoAllocMaxDevices) return fail(FFNRM_ERR_ARG, "device %d beyond the supported %d", dev, kNoAllocMaxDevices);
+    NoAllocScratch scr;
+    int rc = noalloc_scratch(dev, scr);
+    if (rc) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (tokens <= 16) return launch_down_noalloc<16>(down, down_ld, h_hi, h_lo, h_ld, d_model, d_ff, tokens, y_f32, y_f16, status, scr, st);
+    if (tokens <= 32) return launch_down_noalloc<32>(down, down_ld, h_hi, h_lo, h_ld, d_model, d_ff, tokens, y_f32, y_f16, status, scr, st);
+    if (tokens <= 64) return launch_down_noalloc<64>(down, down_ld, h_hi, h_lo, h_ld, d_model, d_ff, tokens, y_f32, y_f16, status, scr, st);
+    return launch_down_noalloc<128>(down, down_ld, h_hi, h_lo, h_ld, d_model, d_ff, tokens, y_f32, y_f16, status, scr, st);
+}
 
 int ffnrm_check_device_error(ffnrm_ctx *ctx, void *stream) {
     if (!ctx) return fail(FFNRM_ERR_ARG, "null context");

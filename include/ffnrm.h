@@ -141,6 +141,28 @@ int ffnrm_cast_f16(const float *src, uint16_t *dst, int64_t n, void *stream);
 /* Device bytes held by loaded weights / workspace (for the bench's byte accounting). */
 int ffnrm_layer_bytes(ffnrm_ctx *ctx, int layer, int64_t *residual_bytes, int64_t *down_bytes);
 
+/* Allocation-free fp16 down projection y[t, o] = sum_f (h_hi + h_lo)[t, f] * down[o, f].
+ * No counterpart in the reference: it exists for callers that cannot allocate device
+ * memory -- code running while a CUDA graph is being captured or inside a graph node,
+ * allocators that forbid cudaMalloc on the serving path, or processes whose memory pool
+ * is fully reserved. It needs no context and calls no cudaMalloc/cudaFree: its split-K
+ * scratch (partial sums for at most 2^21 floats of splits x tokens x d_model, 2048
+ * tile counters and a status word) lives in fixed device arrays of this library, which
+ * every GPU that loads the library holds until the process exits.
+ * Device pointers: down fp16 [d_model][down_ld] row-major (d_ff used columns), h_hi and
+ * h_lo fp16 [tokens][h_ld] whose sum is h (pass zeros as h_lo for plain fp16 h), outputs
+ * y_f32 [tokens][d_model] and/or y_f16; status (optional, 1 int) receives a nonzero code
+ * if the kernel gave up on a bounded pipeline wait. Limits: tokens <= 256, d_model a
+ * multiple of 128 up to 16384, down/h 16-byte aligned, down_ld and h_ld multiples of 8
+ * and >= d_ff; larger requests return FFNRM_ERR_ARG.
+ * The first call on a device looks up the arrays' device addresses (cudaGetSymbolAddress);
+ * make that first call before any stream capture. Every call shares the arrays and clears
+ * the counters it needs, so calls that overlap on the GPU (different streams, or another
+ * thread) race and must be serialised by the caller. */
+int ffnrm_down_project_noalloc(const uint16_t *down, int64_t down_ld, const uint16_t *h_hi, const uint16_t *h_lo,
+                               int64_t h_ld, int d_model, int d_ff, int tokens, float *y_f32, uint16_t *y_f16,
+                               int32_t *status, void *stream);
+
 /* Synchronises `stream` and reports whether any kernel of this context gave up on a
  * bounded pipeline wait since the last check (FFNRM_ERR_TIMEOUT, error word cleared). */
 int ffnrm_check_device_error(ffnrm_ctx *ctx, void *stream);
