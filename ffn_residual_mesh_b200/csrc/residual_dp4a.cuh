@@ -61,7 +61,7 @@ inline size_t residual_smem_bytes(int TT, int D) {
 }
 
 template <int RB, int TT, bool AHALF>
-__global__ void __launch_bounds__(2 * kResWarps * 32) residual_gemv_kernel(const ResidualParams p) {
+__global__ void __launch_bounds__(2 * kResWarps * 32, TT == 1 ? 3 : 2) residual_gemv_kernel(const ResidualParams p) {
     extern __shared__ __align__(16) uint8_t smem[];
     const int G = p.G, D = p.D, F = p.F, T = p.T;
     int8_t *z_sm = reinterpret_cast<int8_t *>(smem);
@@ -110,38 +110,40 @@ __global__ void __launch_bounds__(2 * kResWarps * 32) residual_gemv_kernel(const
 #pragma unroll
     for (int t = 0; t < TT; ++t) acc[t] = 0.f;
 
-    // Loads of kBatch chunks are issued together before any is used, keeping
-    // kBatch x 20 bytes per lane in flight.
-    constexpr int kBatch = 8;
+    // Loads of kBatch chunks are issued together before any is used (kBatch x 20 bytes
+    // per lane in flight); the rare fallback rows load their extra data when used.
+    constexpr int kBatch = 4;
     for (int cb = c_begin; cb < c_end; cb += kBatch) {
-        uint4 wpb[kBatch], whb[kBatch];
+        uint4 wpb[kBatch];
         uint2 wqb[kBatch];
-        float a0b[kBatch], a1b[kBatch], b0b[kBatch], b1b[kBatch];
+        float a0b[kBatch], a1b[kBatch];
 #pragma unroll
         for (int u = 0; u < kBatch; ++u) {
             const int c = cb + u;
             wpb[u] = make_uint4(0, 0, 0, 0);
-            whb[u] = wpb[u];
             wqb[u] = make_uint2(0, 0);
-            a0b[u] = a1b[u] = b0b[u] = b1b[u] = 0.f;
+            a0b[u] = a1b[u] = 0.f;
             if (c < c_end) {
                 const int64_t rec = (int64_t(rb) * C + c) * 32 + lane;
-                if (RB != 1 || flagged) wpb[u] = __ldg(pv.pair + rec);
+                if (RB != 1) wpb[u] = __ldg(pv.pair + rec);
                 if (RB != 2) wqb[u] = __ldg(pv.plane + rec);
                 load_scale2<AHALF>(pv.alpha, rec, a0b[u], a1b[u]);
-                if (flagged) {
-                    whb[u] = __ldg(pv.pair_hi + rec);
-                    load_scale2<AHALF>(pv.beta, rec, b0b[u], b1b[u]);
-                }
             }
         }
 #pragma unroll
         for (int u = 0; u < kBatch; ++u) {
             const int c = cb + u;
             if (c >= c_end) break;
-            const uint4 wp = wpb[u], wh = whb[u];
+            uint4 wp = wpb[u], wh = make_uint4(0, 0, 0, 0);
             const uint2 wq = wqb[u];
-            const float a0 = a0b[u], a1 = a1b[u], b0 = b0b[u], b1 = b1b[u];
+            const float a0 = a0b[u], a1 = a1b[u];
+            float b0 = 0.f, b1 = 0.f;
+            if (flagged) {
+                const int64_t rec = (int64_t(rb) * C + c) * 32 + lane;
+                if (RB == 1) wp = __ldg(pv.pair + rec);
+                wh = __ldg(pv.pair_hi + rec);
+                load_scale2<AHALF>(pv.beta, rec, b0, b1);
+            }
 #pragma unroll
             for (int t = 0; t < TT; ++t) {
                 const uint4 *zv = reinterpret_cast<const uint4 *>(z_sm + t * D + c * 64);

@@ -83,6 +83,15 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint6
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::i8 (u8 A, s8 B, s32 accumulate), issued by one thread.
+__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
 // Arrive on `bar` once all previously issued tcgen05.mma of this thread have completed.
 __device__ __forceinline__ void umma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(smem_u32(bar))
@@ -99,6 +108,49 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
 
+// 32 lanes x 16 consecutive 32-bit TMEM columns <- 16 registers per thread.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(
+            taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
+
+// Make this thread's generic-proxy shared-memory writes visible to the async proxy
+// (tensor core operand reads).
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Packed fp32 pair arithmetic (sm_100): d = a * b + c, d = a + b, d = a * b on float2.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;\n"
+        : "=l"(reinterpret_cast<unsigned long long &>(d))
+        : "l"(reinterpret_cast<unsigned long long &>(a)), "l"(reinterpret_cast<unsigned long long &>(b)),
+          "l"(reinterpret_cast<unsigned long long &>(c)));
+    return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    float2 d;
+    asm("add.rn.f32x2 %0, %1, %2;\n"
+        : "=l"(reinterpret_cast<unsigned long long &>(d))
+        : "l"(reinterpret_cast<unsigned long long &>(a)), "l"(reinterpret_cast<unsigned long long &>(b)));
+    return d;
+}
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+    float2 d;
+    asm("mul.rn.f32x2 %0, %1, %2;\n"
+        : "=l"(reinterpret_cast<unsigned long long &>(d))
+        : "l"(reinterpret_cast<unsigned long long &>(a)), "l"(reinterpret_cast<unsigned long long &>(b)));
+    return d;
+}
+
 // Shared-memory matrix descriptor for a K-major tile written by TMA with 128-byte
 // swizzle: rows of 128 B, 8-row (1024 B) swizzle atoms, so the stride between 8-row
 // groups is 1024 B; the leading offset is unused for swizzled K-major tiles (1);
@@ -112,6 +164,12 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t addr) {
     d |= uint64_t(1) << 46;                     // descriptor version
     d |= uint64_t(2) << 61;                     // SWIZZLE_128B
     return d;
+}
+
+// Instruction descriptor, kind::i8: A unsigned 8-bit (format 0), B signed 8-bit (format 1),
+// s32 accumulate (c_format 2), both K-major, M and N as given.
+__host__ __device__ constexpr uint32_t umma_idesc_u8s8_s32(int M, int N) {
+    return (2u << 4) | (0u << 7) | (1u << 10) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
 }
 
 // Instruction descriptor, kind::f16: A/B fp16 (format 0), f32 accumulate (c_format 1),
