@@ -13,9 +13,12 @@
 //   warp 1 / lane 0 : MMA issuer. Per stage, 4 K=16 steps x (hi, lo) tcgen05.mma into one
 //                     128xN f32 accumulator in tensor memory; tcgen05.commit frees the stage.
 //   warps 0-3       : epilogue. Each warp reads its 32 TMEM lanes (down rows) with
-//                     tcgen05.ld and writes y directly (one slice) or a split-K partial;
-//                     the last CTA of an output tile (atomic ticket) sums the partials
-//                     in slice order (deterministic).
+//                     tcgen05.ld. One slice: y is written directly. Split-K: the slices
+//                     of an output tile run as one thread-block cluster (cluster rank =
+//                     slice); every CTA stages its 128xN partial in its own shared memory,
+//                     and after a cluster barrier CTA r sums rows [32r/S, 32(r+1)/S) x 4
+//                     over the S slices through distributed shared memory, in slice order
+//                     (deterministic, no global scratch).
 // Every mbarrier wait is bounded; on timeout the kernel records an error code in
 // p.err, drains its outstanding copies, frees its TMEM and returns.
 #pragma once
@@ -27,9 +30,9 @@
 
 namespace ffnrm {
 
+constexpr int kDownMaxSplits = 8;  // portable cluster size
+
 struct DownUmmaParams {
-    float *partial;  // [splits][T][D] (split-K only)
-    int *tickets;    // [D/128][ceil(T/N)] zero-initialised, self-resetting
     float *y32;      // [T, D] or null
     __half *y16;     // [T, D] or null
     int *err;        // error word (bounded waits)
@@ -47,7 +50,28 @@ struct DownUmmaCfg {
     static constexpr int stage_bytes = a_bytes + 2 * b_bytes;
     static constexpr int tmem_cols = N < 32 ? 32 : N;
     static constexpr size_t smem = size_t(stages) * stage_bytes + 1024 /*align*/ + 256 /*barriers*/;
+    static_assert(size_t(stages) * stage_bytes >= size_t(N) * kUmmaM * 4, "partial tile reuses the stage ring");
 };
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+// 16 bytes from the shared memory of CTA `rank` of this cluster, at the offset of `local`.
+__device__ __forceinline__ float4 ld_dsmem_f4(const void *local, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(remote) : "r"(sm100::smem_u32(local)), "r"(rank));
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(remote)
+                 : "memory");
+    return v;
+}
 
 template <int N>
 __global__ void __launch_bounds__(128, 1) down_umma_kernel(const __grid_constant__ CUtensorMap tm_w,
@@ -63,13 +87,13 @@ __global__ void __launch_bounds__(128, 1) down_umma_kernel(const __grid_constant
     uint64_t *empty = full + S;
     uint64_t *done = empty + S;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
-    int *flag = reinterpret_cast<int *>(tmem_slot + 1);
 
+    // grid: x = slice (the cluster spans all slices of one output tile), y = row tile,
+    // z = token tile
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * kUmmaM;
-    const int nt = blockIdx.y;
-    const int t0 = nt * N;
-    const int split = blockIdx.z;
+    const int m0 = blockIdx.y * kUmmaM;
+    const int t0 = blockIdx.z * N;
+    const int split = blockIdx.x;
     const int k0 = split * p.kc;
     const int k1 = min(k0 + p.kc, p.F16);
     const int nk = (k1 - k0 + kUmmaK - 1) / kUmmaK;
@@ -129,53 +153,76 @@ __global__ void __launch_bounds__(128, 1) down_umma_kernel(const __grid_constant
     // Epilogue: wait for the accumulator, then each warp drains its 32 TMEM lanes.
     const bool ok = sm100::mbar_wait(done, 0, p.err, sm100::kErrWaitDone);
     sm100::tc_fence_after();
-    const int row = m0 + warp * 32 + lane;
-    const bool direct = p.splits == 1;
-    float *dst = direct ? nullptr : p.partial + int64_t(split) * p.T * p.D;
+    const int row = warp * 32 + lane;
+    const int ntok = min(N, p.T - t0);
+    if (p.splits == 1) {
+        if (ok) {
+#pragma unroll
+            for (int c = 0; c < N; c += 16) {
+                if (c >= ntok) break;
+                uint32_t r[16];
+                sm100::tmem_ld16(tmem + (uint32_t(warp * 32) << 16) + c, r);
+                sm100::tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    if (c + j >= ntok) break;
+                    const float v = __uint_as_float(r[j]);
+                    const int64_t yi = int64_t(t0 + c + j) * p.D + m0 + row;
+                    if (p.y32) p.y32[yi] = v;
+                    if (p.y16) p.y16[yi] = __float2half_rn(v);
+                }
+            }
+        }
+        sm100::tc_fence_before();
+        __syncthreads();
+        if (warp == 0) sm100::tmem_dealloc(tmem, Cfg::tmem_cols);
+        return;
+    }
+
+    // Split-K: stage the partial as [N tokens][128 rows] f32 in the (drained) stage ring.
+    float *part = reinterpret_cast<float *>(tiles);
     if (ok) {
 #pragma unroll
         for (int c = 0; c < N; c += 16) {
+            if (c >= ntok) break;
             uint32_t r[16];
             sm100::tmem_ld16(tmem + (uint32_t(warp * 32) << 16) + c, r);
             sm100::tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int tok = t0 + c + j;
-                if (tok >= p.T) break;
-                const float v = __uint_as_float(r[j]);
-                const int64_t yi = int64_t(tok) * p.D + row;
-                if (direct) {
-                    if (p.y32) p.y32[yi] = v;
-                    if (p.y16) p.y16[yi] = __float2half_rn(v);
-                } else {
-                    dst[yi] = v;
-                }
-            }
+            for (int j = 0; j < 16; ++j) part[(c + j) * kUmmaM + row] = __uint_as_float(r[j]);
         }
     }
     sm100::tc_fence_before();
     __syncthreads();
     if (warp == 0) sm100::tmem_dealloc(tmem, Cfg::tmem_cols);
-    if (direct || !ok) return;
-
-    // split-K: the last CTA of this (row tile, token tile) sums the slices in order
-    __threadfence();
-    __syncthreads();
-    int *ticket = p.tickets + blockIdx.x * gridDim.y + nt;
-    if (threadIdx.x == 0) *flag = atomicAdd(ticket, 1) == p.splits - 1;
-    __syncthreads();
-    if (!*flag) return;
-    __threadfence();
-    const int ntok = min(N, p.T - t0);
-    for (int i = threadIdx.x; i < ntok * kUmmaM; i += blockDim.x) {
-        const int tok = t0 + i / kUmmaM, o = m0 + (i % kUmmaM);
-        const int64_t yi = int64_t(tok) * p.D + o;
-        float v = 0.f;
-        for (int sp = 0; sp < p.splits; ++sp) v += __ldcg(p.partial + int64_t(sp) * p.T * p.D + yi);
-        if (p.y32) p.y32[yi] = v;
-        if (p.y16) p.y16[yi] = __float2half_rn(v);
+    cluster_sync();  // every slice's partial is staged
+    // CTA r of the cluster reduces 4-row units [32r/S, 32(r+1)/S) for all tokens.
+    const int S_ = p.splits;
+    const int rank = int(cluster_ctarank());
+    const int u0 = rank * (kUmmaM / 4) / S_, u1 = (rank + 1) * (kUmmaM / 4) / S_;
+    const int nu = u1 - u0;
+    for (int i = threadIdx.x; i < nu * ntok; i += blockDim.x) {
+        const int t = i / nu, u = u0 + (i - t * nu);
+        const float *src = part + t * kUmmaM + 4 * u;
+        float4 v[kDownMaxSplits];
+#pragma unroll
+        for (int sp = 0; sp < kDownMaxSplits; ++sp)
+            if (sp < S_) v[sp] = ld_dsmem_f4(src, uint32_t(sp));
+        float4 a = v[0];
+#pragma unroll
+        for (int sp = 1; sp < kDownMaxSplits; ++sp)
+            if (sp < S_) a.x += v[sp].x, a.y += v[sp].y, a.z += v[sp].z, a.w += v[sp].w;
+        const int64_t yi = int64_t(t0 + t) * p.D + m0 + 4 * u;
+        if (p.y32) *reinterpret_cast<float4 *>(p.y32 + yi) = a;
+        if (p.y16) {
+            const __half2 lo = __floats2half2_rn(a.x, a.y), hi = __floats2half2_rn(a.z, a.w);
+            uint2 w;
+            w.x = *reinterpret_cast<const uint32_t *>(&lo);
+            w.y = *reinterpret_cast<const uint32_t *>(&hi);
+            *reinterpret_cast<uint2 *>(p.y16 + yi) = w;
+        }
     }
-    if (threadIdx.x == 0) *ticket = 0;  // ready for the next launch on this stream
+    cluster_sync();  // no CTA leaves while a peer still reads its shared memory
 }
 
 }  // namespace ffnrm

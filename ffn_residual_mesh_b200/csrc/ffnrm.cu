@@ -13,6 +13,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <new>
@@ -23,6 +24,7 @@
 #include "ffnrm_common.cuh"
 #include "residual_dp4a.cuh"
 #include "residual_mma.cuh"
+#include "residual_umma.cuh"
 
 namespace {
 
@@ -89,6 +91,20 @@ bool make_fp16_map(CUtensorMap *map, const void *base, uint64_t cols, uint64_t r
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 2-D int8 activations [tokens][d_model] viewed in boxes of 128 codes x box_rows tokens
+// with 128-byte swizzle; tokens past the end read as zero.
+bool make_z_map(CUtensorMap *map, const void *z, uint64_t d_model, uint64_t tokens, uint32_t box_rows) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {d_model, tokens};
+    const cuuint64_t strides[1] = {d_model};
+    const cuuint32_t box[2] = {128, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(z), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace
 
 struct ffnrm_ctx {
@@ -98,12 +114,9 @@ struct ffnrm_ctx {
     std::vector<LayerDev> layers;
     // workspace
     float *res[2] = {nullptr, nullptr};  // [Tm, F]
-    float *partial = nullptr;            // split-K partials, kPartialFloats floats
-    int *tickets = nullptr;              // [D/128][ceil(Tm/16)] split-K arrival counters (self-resetting)
     int *err = nullptr;                  // device error word written by bounded waits
+    bool use_umma = true;                // tcgen05 residual for T >= 5 (FFNRM_RESIDUAL_MMA_SYNC=1 disables)
     CUtensorMap h_map[4][2];             // h hi/lo views for token tiles 16, 32, 64, 128
-    int max_splits = 64;
-    static constexpr size_t kPartialFloats = size_t(2) * 160 * 128 * 128;  // >= splits*T*D whenever splits > 1
     __half *h_hi = nullptr, *h_lo = nullptr;  // [Tm, F16] h = SiLU(g)*u as fp16 hi + lo
     // host-streamed mode staging, double-buffered per call
     int8_t *z_dev[2] = {nullptr, nullptr};
@@ -391,12 +404,41 @@ int launch_residual_mma_nt(ffnrm_ctx *ctx, ffnrm::ResidualParams &p, bool half, 
     return fb ? launch_residual_mma_t<RB, NT, false, true>(ctx, p, st) : launch_residual_mma_t<RB, NT, false, false>(ctx, p, st);
 }
 
-// T <= 4: dp4a GEMV (HBM-bound); larger batches: int8 tensor-core MMA tiles.
+template <int RB, int N, bool AH>
+int launch_residual_umma_t(ffnrm_ctx *ctx, ffnrm::ResidualParams &p, cudaStream_t st) {
+    using Cfg = ffnrm::ResUmmaCfg<RB, N, AH>;
+    const size_t smem = Cfg::smem(p.G);
+    CUtensorMap zm;
+    if (!make_z_map(&zm, p.z, uint64_t(p.D), uint64_t(p.T), N))
+        return fail(FFNRM_ERR_CUDA, "cuTensorMapEncodeTiled rejected the activations");
+    auto kern = p.dots ? ffnrm::residual_umma_kernel<RB, N, AH, true> : ffnrm::residual_umma_kernel<RB, N, AH, false>;
+    FFNRM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+    p.row_blocks = (p.F + 31) / 32;
+    p.err = ctx->err;
+    dim3 grid(unsigned((p.F + ffnrm::kResTileRows - 1) / ffnrm::kResTileRows), unsigned((p.T + N - 1) / N));
+    ProfScope prof(ctx, st, FFNRM_KERNEL_RESIDUAL);
+    kern<<<grid, ffnrm::kResThreads, smem, st>>>(zm, p);
+    ctx->launches++;
+    FFNRM_CUDA(cudaGetLastError());
+    return FFNRM_OK;
+}
+
+template <int RB, int N>
+int launch_residual_umma_n(ffnrm_ctx *ctx, ffnrm::ResidualParams &p, bool half, cudaStream_t st) {
+    return half ? launch_residual_umma_t<RB, N, true>(ctx, p, st) : launch_residual_umma_t<RB, N, false>(ctx, p, st);
+}
+
+// T <= 4: dp4a GEMV (HBM-bound); larger batches: tcgen05 kind::i8 tiles, or mma.sync
+// tiles when fallback tiles need the unsplit codes.
 template <int RB>
 int launch_residual_rb(ffnrm_ctx *ctx, ffnrm::ResidualParams &p, bool half, cudaStream_t st) {
     if (p.T == 1) return launch_residual_tt<RB, 1>(ctx, p, half, st);
     if (p.T == 2) return launch_residual_tt<RB, 2>(ctx, p, half, st);
     if (p.T <= 4) return launch_residual_tt<RB, 4>(ctx, p, half, st);
+    if (p.fallback_tiles == nullptr && ctx->use_umma && ffnrm::ResUmmaCfg<RB, 32, false>::smem(p.G) <= 227 * 1024) {
+        if (p.T <= 16) return launch_residual_umma_n<RB, 16>(ctx, p, half, st);
+        return launch_residual_umma_n<RB, 32>(ctx, p, half, st);
+    }
     if (p.T <= 8) return launch_residual_mma_nt<RB, 1>(ctx, p, half, st);
     if (p.T <= 16) return launch_residual_mma_nt<RB, 2>(ctx, p, half, st);
     return launch_residual_mma_nt<RB, 4>(ctx, p, half, st);  // 32-token tiles (64 would spill)
@@ -438,33 +480,49 @@ int enqueue_residual(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s,
     }
 }
 
+// Launches the down GEMM: split-K slices of one output tile form a thread-block cluster
+// (at most 8) sized so that about two CTAs per SM are busy.
 template <int N>
-int launch_down_t(ffnrm_ctx *ctx, const CUtensorMap &wmap, int map_idx, ffnrm::DownUmmaParams &p, cudaStream_t st) {
+int launch_down_cluster(const CUtensorMap &wm, const CUtensorMap &hm, const CUtensorMap &lm, ffnrm::DownUmmaParams &p,
+                        int num_sms, cudaStream_t st) {
     using Cfg = ffnrm::DownUmmaCfg<N>;
     auto kern = ffnrm::down_umma_kernel<N>;
     FFNRM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::smem)));
     const int occ = Cfg::smem <= 113 * 1024 ? 2 : 1;
     const int mt = p.D / ffnrm::kUmmaM, ntile = (p.T + N - 1) / N;
     const int ksteps = (p.F16 + ffnrm::kUmmaK - 1) / ffnrm::kUmmaK;
-    int splits = std::max(1, std::min(ksteps, occ * ctx->num_sms / (mt * ntile)));
+    int splits = std::max(1, std::min({ksteps, ffnrm::kDownMaxSplits, occ * num_sms / (mt * ntile)}));
     const int kc_steps = (ksteps + splits - 1) / splits;
     splits = (ksteps + kc_steps - 1) / kc_steps;
-    if (splits > 1 && size_t(splits) * p.T * p.D > ffnrm_ctx::kPartialFloats) splits = 1, p.kc = ksteps * ffnrm::kUmmaK;
     p.splits = splits;
-    p.kc = splits == 1 ? ksteps * ffnrm::kUmmaK : kc_steps * ffnrm::kUmmaK;
-    const dim3 grid{unsigned(mt), unsigned(ntile), unsigned(splits)};
-    ProfScope prof(ctx, st, FFNRM_KERNEL_DOWN);
-    kern<<<grid, 128, Cfg::smem, st>>>(wmap, ctx->h_map[map_idx][0], ctx->h_map[map_idx][1], p);
-    ctx->launches++;
-    FFNRM_CUDA(cudaGetLastError());
+    p.kc = kc_steps * ffnrm::kUmmaK;
+    cudaLaunchConfig_t lc{};
+    lc.gridDim = dim3(unsigned(splits), unsigned(mt), unsigned(ntile));
+    lc.blockDim = dim3(128, 1, 1);
+    lc.dynamicSmemBytes = Cfg::smem;
+    lc.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = unsigned(splits);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    FFNRM_CUDA(cudaLaunchKernelEx(&lc, kern, wm, hm, lm, p));
     return FFNRM_OK;
+}
+
+template <int N>
+int launch_down_t(ffnrm_ctx *ctx, const CUtensorMap &wmap, int map_idx, ffnrm::DownUmmaParams &p, cudaStream_t st) {
+    ProfScope prof(ctx, st, FFNRM_KERNEL_DOWN);
+    const int rc = launch_down_cluster<N>(wmap, ctx->h_map[map_idx][0], ctx->h_map[map_idx][1], p, ctx->num_sms, st);
+    ctx->launches++;
+    return rc;
 }
 
 int enqueue_down(ffnrm_ctx *ctx, int layer, int T, float *y32, uint16_t *y16, cudaStream_t st) {
     LayerDev &L = ctx->layers[size_t(layer)];
     ffnrm::DownUmmaParams p{};
-    p.partial = ctx->partial;
-    p.tickets = ctx->tickets;
     p.y32 = y32;
     p.y16 = reinterpret_cast<__half *>(y16);
     p.err = ctx->err;
@@ -480,33 +538,25 @@ int enqueue_down(ffnrm_ctx *ctx, int layer, int T, float *y32, uint16_t *y16, cu
 // ---------------------------------------------------------------------------
 // Allocation-free down projection: scratch in file-scope device arrays
 // ---------------------------------------------------------------------------
-constexpr size_t kNoAllocPartialFloats = size_t(1) << 21;  // split-K partials: 8 MiB per device
-constexpr int kNoAllocTickets = 2048;                      // (d_model/128) x token tiles
 constexpr int kNoAllocMaxTokens = 256;
 constexpr int kNoAllocMaxDModel = 16384;
 constexpr int kNoAllocMaxDevices = 64;
 
 // Held by every GPU that loads this library, until the process exits.
-__device__ __align__(256) float g_noalloc_partial[kNoAllocPartialFloats];
-__device__ __align__(256) int g_noalloc_tickets[kNoAllocTickets];
 __device__ __align__(256) int g_noalloc_status[64];
 
 struct NoAllocScratch {
-    float *partial = nullptr;
-    int *tickets = nullptr;
     int *status = nullptr;
 };
 std::mutex g_noalloc_mutex;
 NoAllocScratch g_noalloc[kNoAllocMaxDevices];
 
-// Device addresses of the scratch arrays on `dev` (the current device), looked up once.
+// Device address of the status word on `dev` (the current device), looked up once.
 int noalloc_scratch(int dev, NoAllocScratch &out) {
     std::lock_guard<std::mutex> lock(g_noalloc_mutex);
     NoAllocScratch &s = g_noalloc[dev];
-    if (!s.partial) {
+    if (!s.status) {
         NoAllocScratch t;
-        FFNRM_CUDA(cudaGetSymbolAddress(reinterpret_cast<void **>(&t.partial), g_noalloc_partial));
-        FFNRM_CUDA(cudaGetSymbolAddress(reinterpret_cast<void **>(&t.tickets), g_noalloc_tickets));
         FFNRM_CUDA(cudaGetSymbolAddress(reinterpret_cast<void **>(&t.status), g_noalloc_status));
         s = t;
     }
@@ -518,42 +568,24 @@ template <int N>
 int launch_down_noalloc(const uint16_t *down, int64_t down_ld, const uint16_t *h_hi, const uint16_t *h_lo,
                         int64_t h_ld, int D, int F, int T, float *y32, uint16_t *y16, int32_t *status,
                         const NoAllocScratch &scr, cudaStream_t st) {
-    using Cfg = ffnrm::DownUmmaCfg<N>;
     CUtensorMap wm, hm, lm;
     if (!make_fp16_map(&wm, down, uint64_t(F), uint64_t(D), uint64_t(down_ld), 128) ||
         !make_fp16_map(&hm, h_hi, uint64_t(F), uint64_t(T), uint64_t(h_ld), N) ||
         !make_fp16_map(&lm, h_lo, uint64_t(F), uint64_t(T), uint64_t(h_ld), N))
         return fail(FFNRM_ERR_CUDA, "cuTensorMapEncodeTiled rejected the down weight or h");
-    auto kern = ffnrm::down_umma_kernel<N>;
-    FFNRM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::smem)));
     int dev = 0, sms = 148;
     FFNRM_CUDA(cudaGetDevice(&dev));
     FFNRM_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    const int occ = Cfg::smem <= 113 * 1024 ? 2 : 1;
-    const int mt = D / ffnrm::kUmmaM, ntile = (T + N - 1) / N;
-    const int F16 = (F + 15) / 16 * 16;
-    const int ksteps = (F16 + ffnrm::kUmmaK - 1) / ffnrm::kUmmaK;
-    int splits = std::max(1, std::min(ksteps, occ * sms / (mt * ntile)));
-    while (splits > 1 && size_t(splits) * T * D > kNoAllocPartialFloats) --splits;
-    const int kc_steps = (ksteps + splits - 1) / splits;
-    splits = (ksteps + kc_steps - 1) / kc_steps;
     ffnrm::DownUmmaParams p{};
-    p.partial = scr.partial;
-    p.tickets = scr.tickets;
     p.y32 = y32;
     p.y16 = reinterpret_cast<__half *>(y16);
     p.err = status ? status : scr.status;
     p.D = D;
-    p.F16 = F16;
+    p.F16 = (F + 15) / 16 * 16;
     p.T = T;
-    p.splits = splits;
-    p.kc = kc_steps * ffnrm::kUmmaK;
-    // The arrays keep the previous call's contents: tickets and status must start at zero.
-    FFNRM_CUDA(cudaMemsetAsync(scr.tickets, 0, size_t(mt) * ntile * sizeof(int), st));
+    // The status word keeps the previous call's value: it must start at zero.
     FFNRM_CUDA(cudaMemsetAsync(p.err, 0, sizeof(int), st));
-    kern<<<dim3(unsigned(mt), unsigned(ntile), unsigned(splits)), 128, Cfg::smem, st>>>(wm, hm, lm, p);
-    FFNRM_CUDA(cudaGetLastError());
-    return FFNRM_OK;
+    return launch_down_cluster<N>(wm, hm, lm, p, sms, st);
 }
 
 }  // namespace
@@ -582,15 +614,12 @@ int ffnrm_create(ffnrm_ctx **out, int device, const ffnrm_config *cfg) {
     ctx->cfg = c;
     ctx->G = c.d_model / 32;
     ctx->layers.resize(size_t(c.n_layers));
+    if (const char *e = std::getenv("FFNRM_RESIDUAL_MMA_SYNC")) ctx->use_umma = std::strcmp(e, "1") != 0;
     cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
     const size_t TF = size_t(c.max_tokens) * c.d_ff, TD = size_t(c.max_tokens) * c.d_model;
     const size_t F16 = (size_t(c.d_ff) + 15) / 16 * 16;
-    const size_t tickets_bytes = size_t(c.d_model / 128) * ((c.max_tokens + 15) / 16) * sizeof(int);
     const int ntiles = (c.d_ff + c.base_tile_rows - 1) / c.base_tile_rows;
     bool ok = cudaMalloc(&ctx->res[0], TF * 4) == cudaSuccess && cudaMalloc(&ctx->res[1], TF * 4) == cudaSuccess &&
-              cudaMalloc(&ctx->partial, ffnrm_ctx::kPartialFloats * 4) == cudaSuccess &&
-              cudaMalloc(&ctx->tickets, tickets_bytes) == cudaSuccess &&
-              cudaMemset(ctx->tickets, 0, tickets_bytes) == cudaSuccess &&
               cudaMalloc(&ctx->err, sizeof(int)) == cudaSuccess && cudaMemset(ctx->err, 0, sizeof(int)) == cudaSuccess &&
               cudaMalloc(&ctx->h_hi, size_t(c.max_tokens) * F16 * 2) == cudaSuccess &&
               cudaMalloc(&ctx->h_lo, size_t(c.max_tokens) * F16 * 2) == cudaSuccess &&
@@ -628,8 +657,6 @@ int ffnrm_destroy(ffnrm_ctx *ctx) {
     for (auto &L : ctx->layers) free_layer(L);
     cudaFree(ctx->res[0]);
     cudaFree(ctx->res[1]);
-    cudaFree(ctx->partial);
-    cudaFree(ctx->tickets);
     cudaFree(ctx->err);
     cudaFree(ctx->h_hi);
     cudaFree(ctx->h_lo);
@@ -727,9 +754,9 @@ int ffnrm_ffn_forward(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s
     if (tokens == 0) return FFNRM_OK;  // empty batch
     if (!z || !s || !gate_base || !up_base) return fail(FFNRM_ERR_ARG, "null device pointer");
     if (!y_f32 && !y_f16) return fail(FFNRM_ERR_ARG, "no output requested");
-    if (!aligned(z, 16) || !aligned(s, 4) || !aligned(gate_base, 4) || !aligned(up_base, 4) || !aligned(y_f32, 4) ||
-        !aligned(y_f16, 2))
-        return fail(FFNRM_ERR_ARG, "z must be 16-byte aligned and s, base sums and outputs element-aligned");
+    if (!aligned(z, 16) || !aligned(s, 4) || !aligned(gate_base, 4) || !aligned(up_base, 4) || !aligned(y_f32, 16) ||
+        !aligned(y_f16, 8))
+        return fail(FFNRM_ERR_ARG, "z and y_f32 must be 16-byte aligned, y_f16 8-byte, s and base sums 4-byte");
     DeviceGuard guard(ctx->device);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if ((rc = enqueue_residual(ctx, layer, z, s, tokens, nullptr, nullptr, nullptr, fallback_tiles, gate_base, up_base,
@@ -849,9 +876,9 @@ int ffnrm_down_project_noalloc(const uint16_t *down, int64_t down_ld, const uint
     if (!down || !h_hi || !h_lo || (!y_f32 && !y_f16)) return fail(FFNRM_ERR_ARG, "null device pointer");
     if (down_ld < d_ff || h_ld < d_ff || down_ld % 8 || h_ld % 8)
         return fail(FFNRM_ERR_ARG, "down_ld and h_ld must be >= d_ff and multiples of 8");
-    if (!aligned(down, 16) || !aligned(h_hi, 16) || !aligned(h_lo, 16) || !aligned(y_f32, 4) || !aligned(y_f16, 2) ||
+    if (!aligned(down, 16) || !aligned(h_hi, 16) || !aligned(h_lo, 16) || !aligned(y_f32, 16) || !aligned(y_f16, 8) ||
         !aligned(status, 4))
-        return fail(FFNRM_ERR_ARG, "down, h_hi and h_lo must be 16-byte aligned");
+        return fail(FFNRM_ERR_ARG, "down, h_hi, h_lo and y_f32 must be 16-byte aligned, y_f16 8-byte");
     if (tokens == 0) return FFNRM_OK;
     int dev = 0;
     FFNRM_CUDA(cudaGetDevice(&dev));

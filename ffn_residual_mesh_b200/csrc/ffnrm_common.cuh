@@ -51,6 +51,20 @@ __device__ __forceinline__ void load_scale2(const void *base, int64_t record, fl
     }
 }
 
+// The same pair of scales from a shared-memory copy of the records.
+template <bool HALF>
+__device__ __forceinline__ void load_scale2_shared(const void *base, int record, float &a0, float &a1) {
+    if constexpr (HALF) {
+        const float2 f = __half22float2(reinterpret_cast<const __half2 *>(base)[record]);
+        a0 = f.x;
+        a1 = f.y;
+    } else {
+        const float2 v = reinterpret_cast<const float2 *>(base)[record];
+        a0 = v.x;
+        a1 = v.y;
+    }
+}
+
 __device__ __forceinline__ bool row_flagged(const uint8_t *tiles, int row, int tile_rows) {
     return tiles != nullptr && tiles[row / tile_rows] != 0;
 }

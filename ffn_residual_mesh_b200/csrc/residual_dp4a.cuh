@@ -31,6 +31,7 @@ struct ResidualParams {
     __half *h_hi, *h_lo;   // [T, F16], F16 = F rounded up to 16 (padding columns written as 0)
     int F, D, G, T, tile_rows, F16;
     int row_blocks;       // ceil(F / 32)
+    int *err;             // pipeline-wait error word (tensor-core kernel), or null
 };
 
 // h = g/(1+exp(-g))*u for one (token, row); flagged rows ignore the base (their g/u

@@ -42,15 +42,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 
 // Waits for the phase of `parity` to complete; after kWaitCycles it records `code` in
 // *err and returns false so the kernel can wind down instead of hanging.
+// The clock is read once per 16 polls.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
+    if (mbar_try_wait(bar, parity)) return true;
     const long long start = clock64();
-    while (!mbar_try_wait(bar, parity)) {
+    while (true) {
+#pragma unroll 1
+        for (int i = 0; i < 16; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
         if (clock64() - start > kWaitCycles) {
             if (err) atomicExch(err, code);
             return false;
         }
     }
-    return true;
 }
 
 // 2-D TMA tiled load into shared memory, completing on `bar` (no multicast).
@@ -62,7 +66,16 @@ __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *m
         : "memory");
 }
 
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+// 1-D bulk copy global -> shared, completing on `bar` (no multicast). Both addresses
+// 16-byte aligned, `bytes` a multiple of 16.
+__device__ __forceinline__ void bulk_load(void *smem_dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                     smem_u32(smem_dst)),
+                 "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before(){ asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
 
 // TMEM allocation by one full warp; the base address lands in *slot (shared memory).
@@ -118,6 +131,41 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
         : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
+
+// 8-column variants of the TMEM load / store above.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};\n" ::"r"(taddr), "r"(r[0]),
+                 "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+}
+// Writes the same 32-bit value into NC consecutive columns (one register for all).
+template <int NC>
+__device__ __forceinline__ void tmem_fill(uint32_t taddr, uint32_t v) {
+    static_assert(NC == 8 || NC == 16, "8 or 16 columns");
+    if constexpr (NC == 8)
+        asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};\n" ::"r"(taddr), "r"(v)
+                     : "memory");
+    else
+        asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};\n" ::"r"(
+                         taddr),
+                     "r"(v)
+                     : "memory");
+}
+template <int NC>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[NC]) {
+    static_assert(NC == 8 || NC == 16, "8 or 16 columns");
+    if constexpr (NC == 8) tmem_ld8(taddr, r); else tmem_ld16(taddr, r);
+}
+template <int NC>
+__device__ __forceinline__ void tmem_st(uint32_t taddr, const uint32_t (&r)[NC]) {
+    static_assert(NC == 8 || NC == 16, "8 or 16 columns");
+    if constexpr (NC == 8) tmem_st8(taddr, r); else tmem_st16(taddr, r);
+}
 
 // Make this thread's generic-proxy shared-memory writes visible to the async proxy
 // (tensor core operand reads).

@@ -109,8 +109,8 @@ int ffnrm_residual(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s, i
  * Device pointers: z, s as above; gate_base/up_base [T,F] f32; fallback_tiles
  * (device, optional) one byte per base tile, nonzero = recompute those rows on
  * the unsplit exact path (needs fallback data loaded; the base of those rows is
- * ignored); y_f32 (optional) [T,D] f32 partial sum over this context's rows;
- * y_f16 (optional) [T,D] fp16. */
+ * ignored); y_f32 (optional, 16-byte aligned) [T,D] f32 partial sum over this
+ * context's rows; y_f16 (optional, 8-byte aligned) [T,D] fp16. */
 int ffnrm_ffn_forward(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s, int tokens,
                       const float *gate_base, const float *up_base, const uint8_t *fallback_tiles,
                       float *y_f32, uint16_t *y_f16, void *stream);
@@ -145,20 +145,22 @@ int ffnrm_layer_bytes(ffnrm_ctx *ctx, int layer, int64_t *residual_bytes, int64_
  * No counterpart in the reference: it exists for callers that cannot allocate device
  * memory -- code running while a CUDA graph is being captured or inside a graph node,
  * allocators that forbid cudaMalloc on the serving path, or processes whose memory pool
- * is fully reserved. It needs no context and calls no cudaMalloc/cudaFree: its split-K
- * scratch (partial sums for at most 2^21 floats of splits x tokens x d_model, 2048
- * tile counters and a status word) lives in fixed device arrays of this library, which
- * every GPU that loads the library holds until the process exits.
+ * is fully reserved. It needs no context and calls no cudaMalloc/cudaFree: split-K
+ * partial sums are reduced across a thread-block cluster in shared memory, and the
+ * only scratch, the default status word, is a fixed device array of this library,
+ * which every GPU that loads the library holds until the process exits.
  * Device pointers: down fp16 [d_model][down_ld] row-major (d_ff used columns), h_hi and
  * h_lo fp16 [tokens][h_ld] whose sum is h (pass zeros as h_lo for plain fp16 h), outputs
- * y_f32 [tokens][d_model] and/or y_f16; status (optional, 1 int) receives a nonzero code
- * if the kernel gave up on a bounded pipeline wait. Limits: tokens <= 256, d_model a
- * multiple of 128 up to 16384, down/h 16-byte aligned, down_ld and h_ld multiples of 8
- * and >= d_ff; larger requests return FFNRM_ERR_ARG.
- * The first call on a device looks up the arrays' device addresses (cudaGetSymbolAddress);
- * make that first call before any stream capture. Every call shares the arrays and clears
- * the counters it needs, so calls that overlap on the GPU (different streams, or another
- * thread) race and must be serialised by the caller. */
+ * y_f32 [tokens][d_model] (16-byte aligned) and/or y_f16 (8-byte aligned); status
+ * (optional, 1 int) receives a nonzero code if the kernel gave up on a bounded pipeline
+ * wait. Limits: tokens <= 256, d_model a multiple of 128 up to 16384, down/h 16-byte
+ * aligned, down_ld and h_ld multiples of 8 and >= d_ff; larger requests return
+ * FFNRM_ERR_ARG.
+ * The first call on a device looks up the status word's device address
+ * (cudaGetSymbolAddress); make that first call before any stream capture. Calls that
+ * pass status = NULL share the default status word and clear it, so such calls that
+ * overlap on the GPU (different streams, or another thread) race on it and must be
+ * serialised by the caller (or pass their own status word). */
 int ffnrm_down_project_noalloc(const uint16_t *down, int64_t down_ld, const uint16_t *h_hi, const uint16_t *h_lo,
                                int64_t h_ld, int d_model, int d_ff, int tokens, float *y_f32, uint16_t *y_f16,
                                int32_t *status, void *stream);

@@ -345,3 +345,52 @@ def test_eager_call_after_capture(cuda):
     torch.cuda.synchronize()
     g.close()
     ctx.close()
+
+
+@pytest.mark.parametrize("T,F,r,half_alpha", [(5, 200, 2, True), (16, 64, 1, True), (17, 1000, 3, False),
+                                              (64, 1000, 2, True), (100, 130, 2, False), (33, 333, 1, False)])
+def test_tensor_core_residual_tiles(T, F, r, half_alpha, cuda, monkeypatch):
+    """Batches of 5+ tokens without fallback tiles run on the tcgen05 kind::i8 tiles
+    (64 gate + 64 up rows x 16 or 32 tokens): group dots bit-exact against the oracle
+    and against the mma.sync tiles, residuals and the forward output within tolerance,
+    for r = 1/2/3, fp16-exact and f32 alpha, ragged d_ff and partial token tiles."""
+    import torch
+    from ffn_residual_mesh_b200 import synth
+    from ffn_residual_mesh_b200.engine import LayerSpec, ResidualMesh
+    D = 1024
+    L = synth.make_layer(40 + T, F, D)
+    if not half_alpha:  # not representable in fp16: the kernels read f32 scales
+        L.gate_alpha[:] = L.gate_alpha * np.float32(1 + 2 ** -20)
+        L.up_alpha[:] = L.up_alpha * np.float32(1 + 2 ** -20)
+    _, z, s = synth.make_activations(41 + T, T, D)
+    gb = O.host_base(L.gate_codes, L.gate_alpha, L.gate_beta, z, s, r)
+    ub = O.host_base(L.up_codes, L.up_alpha, L.up_beta, z, s, r)
+    spec = LayerSpec(L.gate_codes, L.up_codes, L.gate_alpha, L.up_alpha, L.down, L.gate_beta, L.up_beta)
+    results = {}
+    for legacy in ("0", "1"):
+        monkeypatch.setenv("FFNRM_RESIDUAL_MMA_SYNC", legacy)
+        ctx = ResidualMesh(D, F, r, 1, T)
+        ctx.load_layer(0, spec)
+        g = torch.empty(T, F, device=cuda)
+        u = torch.empty_like(g)
+        dots = torch.full((2, T, F, D // 32), -7, dtype=torch.int32, device=cuda)
+        ctx.residual(0, dev(z, cuda), dev(s, cuda), g, u, dots)
+        y32 = torch.empty(T, D, device=cuda)
+        ctx.forward(0, dev(z, cuda), dev(s, cuda), dev(gb.astype(np.float32), cuda), dev(ub.astype(np.float32), cuda),
+                    y32=y32)
+        torch.cuda.synchronize()
+        ctx.check_device_error()
+        results[legacy] = (dots.cpu().numpy(), g.cpu().numpy(), u.cpu().numpy(), y32.cpu().numpy())
+        ctx.close()
+    dots, g, u, y = results["0"]
+    mask = (1 << r) - 1
+    np.testing.assert_array_equal(dots[0], O.group_dots(L.gate_codes & mask, z))
+    np.testing.assert_array_equal(dots[1], O.group_dots(L.up_codes & mask, z))
+    np.testing.assert_array_equal(dots, results["1"][0])
+    close_rows(g, O.residual(L.gate_codes, L.gate_alpha, z, s, r), rtol=2e-5)
+    close_rows(u, O.residual(L.up_codes, L.up_alpha, z, s, r), rtol=2e-5)
+    ref = O.ffn_forward(L.gate_codes, L.up_codes, L.gate_alpha, L.up_alpha, L.gate_beta, L.up_beta, L.down, z, s, r,
+                        gate_base=gb, up_base=ub)
+    assert rel_l2(y, ref["y"]) < 1e-5
+    assert np.abs(y - ref["y"]).max() < Y_MAX_ABS
+    assert rel_l2(y, results["1"][3]) < 1e-5
