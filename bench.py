@@ -287,6 +287,15 @@ def run_ours(args, cfg, rank, world, local_rank):
     mesh.profile(False)
     launches = launches_per_step * args.steps
 
+    res_bytes_layer, down_bytes_layer = mesh.layer_bytes(0)
+    D, G = cfg.d_model, cfg.d_model // 32
+
+    def alg_bytes(T):
+        # residual: codes + alpha, activations and scales, both base sums in, h (fp16 hi + lo) out;
+        # down: fp16 down weight, h (hi + lo) in, y (fp16) out
+        return {"residual": res_bytes_layer + T * D + T * G * 4 + 2 * T * F * 4 + T * F * 4,
+                "down": down_bytes_layer + T * F * 4 + T * D * 2}
+
     per_batch = {}
     for T in cfg.tokens:
         def one_batch(T=T):
@@ -299,6 +308,29 @@ def run_ours(args, cfg, rank, world, local_rank):
                              "us_per_layer": 1e3 * ms_b / args.steps / cfg.layers}
         if runner:
             runner.close()
+        # per-kernel device time for this batch size alone
+        mesh.profile(True)
+        pk = {"residual": [0.0, 0], "down": [0.0, 0]}
+        g_b = StepGraph(one_batch, warmup=0) if use_graphs else None
+        for _ in range(args.steps):
+            g_b.replay() if g_b else one_batch()
+            if g_b:
+                for k, (ms, n) in mesh.profile_read().items():
+                    if k in pk:
+                        pk[k][0] += ms
+                        pk[k][1] += n
+        if not g_b:
+            for k, (ms, n) in mesh.profile_read().items():
+                if k in pk:
+                    pk[k] = [ms, n]
+        else:
+            g_b.close()
+        mesh.profile(False)
+        ab = alg_bytes(T)
+        for k, (ms, n) in pk.items():
+            if n:
+                us = 1e3 * ms / n
+                per_batch[str(T)][k] = {"us_per_launch": us, "achieved_gbs": ab[k] / (us * 1e-6) / 1e9}
     if use_graphs:
         g_dev.close()
         g_e2e.close()
@@ -309,14 +341,10 @@ def run_ours(args, cfg, rank, world, local_rank):
     e2e_value = tokens_step * args.steps / (e2e_ms / 1e3)
 
     # roofline: algorithmic bytes per launch / live CUDA-event time per launch
-    res_bytes_layer, down_bytes_layer = mesh.layer_bytes(0)
-    D, G = cfg.d_model, cfg.d_model // 32
     alg = {"residual": 0, "down": 0}
     for T in cfg.tokens:
-        # codes + alpha, activations and scales, both base sums in, h (fp16 hi + lo) out
-        alg["residual"] += cfg.layers * (res_bytes_layer + T * D + T * G * 4 + 2 * T * F * 4 + T * F * 4)
-        # fp16 down weight, h (hi + lo) in, y (fp16) out
-        alg["down"] += cfg.layers * (down_bytes_layer + T * F * 4 + T * D * 2)
+        for k, v in alg_bytes(T).items():
+            alg[k] += cfg.layers * v
     alg = {k: v * args.steps for k, v in alg.items()}
     peak, peak_kind = peaks()
     kern = {}

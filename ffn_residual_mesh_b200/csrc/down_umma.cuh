@@ -7,9 +7,10 @@
 //
 // y[t, o] = sum_f h[t, f] * Wd[o, f] is a GEMM with M = d_model (down rows), N = tokens,
 // K = d_ff. CTA tile: 128 down rows x N tokens x a split-K slice of d_ff.
-//   warp 0 / lane 0 : TMA producer. Per 64-column K step it loads the 128x64 fp16 tile of
+//   warp 0          : TMA producer. Per 64-column K step it loads the 128x64 fp16 tile of
 //                     Wd and the Nx64 tiles of h hi and lo (128-byte swizzle) into a
-//                     kStages-deep shared-memory ring, completing on full[s].
+//                     shared-memory ring, completing on full[s]; a batch of S/2 steps is
+//                     issued at once, one copy per lane.
 //   warp 1 / lane 0 : MMA issuer. Per stage, 4 K=16 steps x (hi, lo) tcgen05.mma into one
 //                     128xN f32 accumulator in tensor memory; tcgen05.commit frees the stage.
 //   warps 0-3       : epilogue. Each warp reads its 32 TMEM lanes (down rows) with
@@ -112,23 +113,35 @@ __global__ void __launch_bounds__(128, 1) down_umma_kernel(const __grid_constant
     sm100::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 0 && lane == 0) {
-        // TMA producer
+    if (warp == 0) {
+        // TMA producer warp. A thread's copies do not overlap one another, so K steps are
+        // issued in batches of max(1, S/2) with one copy per lane (lane 3k + op: W, h hi
+        // or h lo of the batch's k-th step), keeping a whole batch in flight.
+        const int B = S / 2 > 1 ? S / 2 : 1;
+        const int k = lane / 3, op = lane - 3 * (lane / 3);
         int issued = 0;
-        for (int it = 0; it < nk; ++it) {
-            const int s = it % S;
-            if (!sm100::mbar_wait(empty + s, ((it / S) & 1) ^ 1, p.err, sm100::kErrWaitEmpty)) break;
-            uint8_t *st = tiles + s * Cfg::stage_bytes;
-            sm100::mbar_arrive_expect_tx(full + s, Cfg::stage_bytes);
-            const int kx = k0 + it * kUmmaK;
-            sm100::tma_load_2d(st, &tm_w, kx, m0, full + s);
-            sm100::tma_load_2d(st + Cfg::a_bytes, &tm_hi, kx, t0, full + s);
-            sm100::tma_load_2d(st + Cfg::a_bytes + Cfg::b_bytes, &tm_lo, kx, t0, full + s);
-            ++issued;
+        for (int it0 = 0; it0 < nk; it0 += B) {
+            const int nb = min(B, nk - it0);
+            const int it = it0 + k, s = it % S;
+            bool ok = true;
+            if (k < nb && op == 0) {
+                ok = sm100::mbar_wait(empty + s, ((it / S) & 1) ^ 1, p.err, sm100::kErrWaitEmpty);
+                if (ok) sm100::mbar_arrive_expect_tx(full + s, Cfg::stage_bytes);
+            }
+            if (!__all_sync(0xffffffffu, ok)) break;
+            if (k < nb) {
+                uint8_t *st = tiles + s * Cfg::stage_bytes;
+                const int kx = k0 + it * kUmmaK;
+                const CUtensorMap *map = op == 0 ? &tm_w : op == 1 ? &tm_hi : &tm_lo;
+                uint8_t *dst = op == 0 ? st : st + Cfg::a_bytes + (op - 1) * Cfg::b_bytes;
+                sm100::tma_load_2d(dst, map, kx, op == 0 ? m0 : t0, full + s);
+            }
+            issued = it0 + nb;
         }
         // No copy may still be in flight when the CTA exits: wait for the last stages.
-        for (int it = max(0, issued - S); it < issued; ++it)
-            sm100::mbar_wait(full + it % S, (it / S) & 1, p.err, sm100::kErrWaitFull);
+        if (lane == 0)
+            for (int it = max(0, issued - S); it < issued; ++it)
+                sm100::mbar_wait(full + it % S, (it / S) & 1, p.err, sm100::kErrWaitFull);
     } else if (warp == 1 && lane == 0) {
         // MMA issuer
         constexpr uint32_t idesc = sm100::umma_idesc_f16_f32(kUmmaM, N);

@@ -24,7 +24,7 @@
 #include "ffnrm_common.cuh"
 #include "residual_dp4a.cuh"
 #include "residual_mma.cuh"
-#include "residual_umma.cuh"
+#include "residual_tc.cuh"
 
 namespace {
 
@@ -57,8 +57,15 @@ struct LayerDev {
     bool loaded = false;
     bool scales_half = true;
     bool has_fallback = false;
-    DevBuf pair[2], plane[2], pair_hi[2], alpha[2], beta[2], down;
-    CUtensorMap down_map;  // TMA view of down [D][F16] fp16, box 64 x 128, 128-byte swizzle
+    // code records, bit-plane records, fallback high pairs and scales of both projections
+    // in the row-tiled layout of ffnrm_common.cuh (a projection's view starts 64 records in
+    // for up)
+    DevBuf pair, plane, pair_hi, alpha, beta, down;
+    // low codes, one byte each, rows [128*rt, 128*rt+64) gate rows of tile rt then its up
+    // rows: the tensor-core A operand (built when batches of more than kGemvMaxTokens fit)
+    DevBuf codes8;
+    CUtensorMap codes8_map;  // box 128 codes x 128 rows, 128-byte swizzle
+    CUtensorMap down_map;    // TMA view of down [D][F16] fp16, box 64 x 128, 128-byte swizzle
 };
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -177,41 +184,50 @@ int upload(DevBuf &b, const void *host, size_t bytes) {
 
 // Pack bits [shift, shift+1] of codes [F, D] into the interleaved pair layout
 // [F32][G/2][32][16 B] (see ffnrm_common.cuh). Padding rows are zero.
-void pack_pair_il(const uint8_t *q, int shift, int64_t F, int64_t D, std::vector<uint8_t> &out) {
-    const int64_t F32 = (F + 31) / 32, C = D / 64;
-    out.assign(size_t(F32 * C * 32 * 16), 0);
-    for (int64_t r = 0; r < F; ++r) {
-        const uint8_t *src = q + r * D;
-        for (int64_t c = 0; c < C; ++c) {
-            uint32_t *rec = reinterpret_cast<uint32_t *>(out.data() + (((r / 32) * C + c) * 32 + (r % 32)) * 16);
-            for (int j = 0; j < 4; ++j) {
-                const uint8_t *codes = src + 64 * c + 16 * j;  // group 2c + (j>>1), half j&1
-                uint32_t w = 0;
-                for (int i = 0; i < 4; ++i)
-                    for (int b = 0; b < 4; ++b) w |= uint32_t((codes[4 * i + b] >> shift) & 3) << (8 * b + 2 * i);
-                rec[j] = w;
-            }
-        }
-    }
+// Record of projection `proj`, row r, chunk c in the row-tiled layout.
+int64_t tiled_record(int proj, int64_t r, int64_t C, int64_t c) {
+    return ((r / 64) * C + c) * 128 + proj * 64 + (r % 64);
 }
 
-// Pack bit `bit` of codes [F, D] into the interleaved plane layout [F32][G/2][32][8 B].
-void pack_plane_il(const uint8_t *q, int bit, int64_t F, int64_t D, std::vector<uint8_t> &out) {
-    const int64_t F32 = (F + 31) / 32, C = D / 64;
-    out.assign(size_t(F32 * C * 32 * 8), 0);
-    for (int64_t r = 0; r < F; ++r) {
-        const uint8_t *src = q + r * D;
-        for (int64_t c = 0; c < C; ++c) {
-            uint32_t *rec = reinterpret_cast<uint32_t *>(out.data() + (((r / 32) * C + c) * 32 + (r % 32)) * 8);
-            for (int j = 0; j < 2; ++j) {
-                const uint8_t *codes = src + 64 * c + 32 * j;
-                uint32_t w = 0;
-                for (int i = 0; i < 8; ++i)
-                    for (int b = 0; b < 4; ++b) w |= uint32_t((codes[4 * i + b] >> bit) & 1) << (8 * b + i);
-                rec[j] = w;
+// Pack bits shift..shift+1 of both projections' codes [F, D] into pair records
+// [F64][G/2][2][64][16 B].
+void pack_pair_tiles(const uint8_t *const q[2], int shift, int64_t F, int64_t D, std::vector<uint8_t> &out) {
+    const int64_t F64 = (F + 63) / 64, C = D / 64;
+    out.assign(size_t(F64 * C * 128 * 16), 0);
+    for (int proj = 0; proj < 2; ++proj)
+        for (int64_t r = 0; r < F; ++r) {
+            const uint8_t *src = q[proj] + r * D;
+            for (int64_t c = 0; c < C; ++c) {
+                uint32_t *rec = reinterpret_cast<uint32_t *>(out.data() + tiled_record(proj, r, C, c) * 16);
+                for (int j = 0; j < 4; ++j) {
+                    const uint8_t *codes = src + 64 * c + 16 * j;  // group 2c + (j>>1), half j&1
+                    uint32_t w = 0;
+                    for (int i = 0; i < 4; ++i)
+                        for (int b = 0; b < 4; ++b) w |= uint32_t((codes[4 * i + b] >> shift) & 3) << (8 * b + 2 * i);
+                    rec[j] = w;
+                }
             }
         }
-    }
+}
+
+// Pack bit `bit` of both projections' codes [F, D] into plane records [F64][G/2][2][64][8 B].
+void pack_plane_tiles(const uint8_t *const q[2], int bit, int64_t F, int64_t D, std::vector<uint8_t> &out) {
+    const int64_t F64 = (F + 63) / 64, C = D / 64;
+    out.assign(size_t(F64 * C * 128 * 8), 0);
+    for (int proj = 0; proj < 2; ++proj)
+        for (int64_t r = 0; r < F; ++r) {
+            const uint8_t *src = q[proj] + r * D;
+            for (int64_t c = 0; c < C; ++c) {
+                uint32_t *rec = reinterpret_cast<uint32_t *>(out.data() + tiled_record(proj, r, C, c) * 8);
+                for (int j = 0; j < 2; ++j) {
+                    const uint8_t *codes = src + 64 * c + 32 * j;
+                    uint32_t w = 0;
+                    for (int i = 0; i < 8; ++i)
+                        for (int b = 0; b < 4; ++b) w |= uint32_t((codes[4 * i + b] >> bit) & 1) << (8 * b + i);
+                    rec[j] = w;
+                }
+            }
+        }
 }
 
 // Decode one projection's input codes into full / low code bytes [F, D].
@@ -270,13 +286,14 @@ bool all_half_exact(const float *v, int64_t n) {
 }
 
 // Per-group scales [F, G] -> interleaved [F32][G/2][32][2] (fp16 or f32).
-int upload_scales(DevBuf &b, const float *v, int64_t F, int64_t G, bool as_half) {
-    const int64_t F32 = (F + 31) / 32, C = G / 2, n = F32 * C * 32 * 2;
+// Both projections' scales [F, G] -> [F64][G/2][2][64][2], fp16 when lossless.
+int upload_scales(DevBuf &b, const float *const v[2], int64_t F, int64_t G, bool as_half) {
+    const int64_t F64 = (F + 63) / 64, C = G / 2, n = F64 * C * 128 * 2;
     std::vector<float> il(size_t(n), 0.f);
-    for (int64_t r = 0; r < F; ++r)
-        for (int64_t c = 0; c < C; ++c)
-            for (int e = 0; e < 2; ++e)
-                il[size_t((((r / 32) * C + c) * 32 + (r % 32)) * 2 + e)] = v[r * G + 2 * c + e];
+    for (int proj = 0; proj < 2; ++proj)
+        for (int64_t r = 0; r < F; ++r)
+            for (int64_t c = 0; c < C; ++c)
+                for (int e = 0; e < 2; ++e) il[size_t(tiled_record(proj, r, C, c) * 2 + e)] = v[proj][r * G + 2 * c + e];
     if (!as_half) return upload(b, il.data(), size_t(n) * 4);
     std::vector<__half> h{};
     h.resize(size_t(n));
@@ -292,13 +309,37 @@ int upload_down(DevBuf &b, const uint16_t *down, int64_t ld, int64_t F, int64_t 
     return upload(b, rm.data(), rm.size() * 2);
 }
 
+// Low codes of both projections [F, D] -> [F64 * 128][D] bytes, tile rows stacked gate
+// then up.
+void pack_codes8(const uint8_t *const q[2], int64_t F, int64_t D, std::vector<uint8_t> &out) {
+    const int64_t F64 = (F + 63) / 64;
+    out.assign(size_t(F64 * 128 * D), 0);
+    for (int proj = 0; proj < 2; ++proj)
+        for (int64_t r = 0; r < F; ++r)
+            std::memcpy(out.data() + ((r / 64) * 128 + proj * 64 + r % 64) * D, q[proj] + r * D, size_t(D));
+}
+
+// 2-D u8 tensor [rows][cols] in boxes of 128 x box_rows with 128-byte swizzle.
+bool make_u8_map(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows, uint32_t box_rows) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols};
+    const cuuint32_t box[2] = {128, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 void free_layer(LayerDev &L) {
-    for (int p = 0; p < 2; ++p) {
-        dev_free(L.pair[p]);
-        dev_free(L.plane[p]);
-        dev_free(L.pair_hi[p]);
-        dev_free(L.alpha[p]);
-        dev_free(L.beta[p]);
+    {
+        dev_free(L.pair);
+        dev_free(L.plane);
+        dev_free(L.pair_hi);
+        dev_free(L.alpha);
+        dev_free(L.beta);
+        dev_free(L.codes8);
     }
     dev_free(L.down);
     L.loaded = false;
@@ -404,40 +445,37 @@ int launch_residual_mma_nt(ffnrm_ctx *ctx, ffnrm::ResidualParams &p, bool half, 
     return fb ? launch_residual_mma_t<RB, NT, false, true>(ctx, p, st) : launch_residual_mma_t<RB, NT, false, false>(ctx, p, st);
 }
 
-template <int RB, int N, bool AH>
-int launch_residual_umma_t(ffnrm_ctx *ctx, ffnrm::ResidualParams &p, cudaStream_t st) {
-    using Cfg = ffnrm::ResUmmaCfg<RB, N, AH>;
-    const size_t smem = Cfg::smem(p.G);
+template <int N, bool AH>
+int launch_residual_tc_t(ffnrm_ctx *ctx, const LayerDev &L, ffnrm::ResidualParams &p, cudaStream_t st) {
+    using Cfg = ffnrm::ResTcCfg<N, AH>;
+    const int stages = Cfg::stages_for(p.G);
+    const size_t smem = Cfg::smem(p.G, stages);
     CUtensorMap zm;
     if (!make_z_map(&zm, p.z, uint64_t(p.D), uint64_t(p.T), N))
         return fail(FFNRM_ERR_CUDA, "cuTensorMapEncodeTiled rejected the activations");
-    auto kern = p.dots ? ffnrm::residual_umma_kernel<RB, N, AH, true> : ffnrm::residual_umma_kernel<RB, N, AH, false>;
+    auto kern = p.dots ? ffnrm::residual_tc_kernel<N, AH, true> : ffnrm::residual_tc_kernel<N, AH, false>;
     FFNRM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
     p.row_blocks = (p.F + 31) / 32;
     p.err = ctx->err;
-    dim3 grid(unsigned((p.F + ffnrm::kResTileRows - 1) / ffnrm::kResTileRows), unsigned((p.T + N - 1) / N));
+    dim3 grid(unsigned((p.F + ffnrm::kTcTileRows - 1) / ffnrm::kTcTileRows), unsigned((p.T + N - 1) / N));
     ProfScope prof(ctx, st, FFNRM_KERNEL_RESIDUAL);
-    kern<<<grid, ffnrm::kResThreads, smem, st>>>(zm, p);
+    kern<<<grid, ffnrm::kTcThreads, smem, st>>>(L.codes8_map, zm, p, stages);
     ctx->launches++;
     FFNRM_CUDA(cudaGetLastError());
     return FFNRM_OK;
 }
 
-template <int RB, int N>
-int launch_residual_umma_n(ffnrm_ctx *ctx, ffnrm::ResidualParams &p, bool half, cudaStream_t st) {
-    return half ? launch_residual_umma_t<RB, N, true>(ctx, p, st) : launch_residual_umma_t<RB, N, false>(ctx, p, st);
-}
-
-// T <= 4: dp4a GEMV (HBM-bound); larger batches: tcgen05 kind::i8 tiles, or mma.sync
-// tiles when fallback tiles need the unsplit codes.
+// T <= 4: dp4a GEMV (HBM-bound); larger batches: tcgen05 kind::i8 tiles on the byte
+// codes, or mma.sync tiles when fallback tiles need the unsplit codes.
 template <int RB>
-int launch_residual_rb(ffnrm_ctx *ctx, ffnrm::ResidualParams &p, bool half, cudaStream_t st) {
+int launch_residual_rb(ffnrm_ctx *ctx, const LayerDev &L, ffnrm::ResidualParams &p, bool half, cudaStream_t st) {
     if (p.T == 1) return launch_residual_tt<RB, 1>(ctx, p, half, st);
     if (p.T == 2) return launch_residual_tt<RB, 2>(ctx, p, half, st);
     if (p.T <= 4) return launch_residual_tt<RB, 4>(ctx, p, half, st);
-    if (p.fallback_tiles == nullptr && ctx->use_umma && ffnrm::ResUmmaCfg<RB, 32, false>::smem(p.G) <= 227 * 1024) {
-        if (p.T <= 16) return launch_residual_umma_n<RB, 16>(ctx, p, half, st);
-        return launch_residual_umma_n<RB, 32>(ctx, p, half, st);
+    if (p.fallback_tiles == nullptr && L.codes8.ptr && ctx->use_umma &&
+        ffnrm::ResTcCfg<32, false>::smem(p.G, 2) <= 227 * 1024) {
+        if (p.T <= 16) return half ? launch_residual_tc_t<16, true>(ctx, L, p, st) : launch_residual_tc_t<16, false>(ctx, L, p, st);
+        return half ? launch_residual_tc_t<32, true>(ctx, L, p, st) : launch_residual_tc_t<32, false>(ctx, L, p, st);
     }
     if (p.T <= 8) return launch_residual_mma_nt<RB, 1>(ctx, p, half, st);
     if (p.T <= 16) return launch_residual_mma_nt<RB, 2>(ctx, p, half, st);
@@ -453,9 +491,16 @@ int enqueue_residual(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s,
     if (tiles && !L.has_fallback)
         return fail(FFNRM_ERR_STATE, "fallback tiles given but layer %d was loaded without fallback data", layer);
     ffnrm::ResidualParams p{};
-    for (int q = 0; q < 2; ++q)
-        p.proj[q] = ffnrm::ProjView{static_cast<const uint4 *>(L.pair[q].ptr), static_cast<const uint2 *>(L.plane[q].ptr),
-                                    static_cast<const uint4 *>(L.pair_hi[q].ptr), L.alpha[q].ptr, L.beta[q].ptr};
+    for (int q = 0; q < 2; ++q) {
+        // a projection's view starts 64 records into each tile's run (0 for gate, 64 for up)
+        const int64_t o = 64 * q, sb = L.scales_half ? 4 : 8;
+        auto at = [](const DevBuf &b, int64_t bytes) -> const void * {
+            return b.ptr ? static_cast<const uint8_t *>(b.ptr) + bytes : nullptr;
+        };
+        p.proj[q] = ffnrm::ProjView{static_cast<const uint4 *>(at(L.pair, o * 16)), static_cast<const uint2 *>(at(L.plane, o * 8)),
+                                    static_cast<const uint4 *>(at(L.pair_hi, o * 16)), at(L.alpha, o * sb),
+                                    at(L.beta, o * sb)};
+    }
     p.z = z;
     p.s = s;
     p.out[0] = gate_res;
@@ -474,9 +519,9 @@ int enqueue_residual(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s,
     p.tile_rows = ctx->cfg.base_tile_rows;
     const int r = ctx->cfg.residual_bits;
     switch (r) {
-        case 1: return launch_residual_rb<1>(ctx, p, L.scales_half, st);
-        case 2: return launch_residual_rb<2>(ctx, p, L.scales_half, st);
-        default: return launch_residual_rb<3>(ctx, p, L.scales_half, st);
+        case 1: return launch_residual_rb<1>(ctx, L, p, L.scales_half, st);
+        case 2: return launch_residual_rb<2>(ctx, L, p, L.scales_half, st);
+        default: return launch_residual_rb<3>(ctx, L, p, L.scales_half, st);
     }
 }
 
@@ -697,27 +742,36 @@ int ffnrm_load_layer(ffnrm_ctx *ctx, int layer, const ffnrm_layer_weights *w) {
     const uint8_t *high[2] = {w->gate_high, w->up_high};
     const float *alpha[2] = {w->gate_alpha, w->up_alpha};
     const float *beta[2] = {w->gate_beta, w->up_beta};
-    std::vector<uint8_t> lo, full, packed;
+    std::vector<uint8_t> lo[2], full[2], packed;
+    bool have_full[2] = {false, false};
     int rc = FFNRM_OK;
-    for (int q = 0; q < 2 && rc == FFNRM_OK; ++q) {
-        bool have_full = false;
-        rc = decode_codes(w, codes[q], L.has_fallback ? high[q] : nullptr, r, F, D, lo, full, have_full);
-        if (rc) break;
-        if (r != 1 || L.has_fallback) {
-            // bits 0-1 of the full code equal the low two residual bits for r >= 2
-            pack_pair_il(have_full ? full.data() : lo.data(), 0, F, D, packed);
-            if ((rc = upload(L.pair[q], packed.data(), packed.size()))) break;
-        }
-        if (r != 2) {
-            pack_plane_il(lo.data(), r == 1 ? 0 : 2, F, D, packed);
-            if ((rc = upload(L.plane[q], packed.data(), packed.size()))) break;
-        }
-        if (L.has_fallback) {
-            pack_pair_il(full.data(), 2, F, D, packed);
-            if ((rc = upload(L.pair_hi[q], packed.data(), packed.size()))) break;
-            if ((rc = upload_scales(L.beta[q], beta[q], F, G, L.scales_half))) break;
-        }
-        rc = upload_scales(L.alpha[q], alpha[q], F, G, L.scales_half);
+    for (int q = 0; q < 2 && rc == FFNRM_OK; ++q)
+        rc = decode_codes(w, codes[q], L.has_fallback ? high[q] : nullptr, r, F, D, lo[q], full[q], have_full[q]);
+    if (rc == FFNRM_OK && (r != 1 || L.has_fallback)) {
+        // bits 0-1 of the full code equal the low two residual bits for r >= 2
+        const uint8_t *src[2] = {have_full[0] ? full[0].data() : lo[0].data(), have_full[1] ? full[1].data() : lo[1].data()};
+        pack_pair_tiles(src, 0, F, D, packed);
+        rc = upload(L.pair, packed.data(), packed.size());
+    }
+    if (rc == FFNRM_OK && r != 2) {
+        const uint8_t *src[2] = {lo[0].data(), lo[1].data()};
+        pack_plane_tiles(src, r == 1 ? 0 : 2, F, D, packed);
+        rc = upload(L.plane, packed.data(), packed.size());
+    }
+    if (rc == FFNRM_OK && L.has_fallback) {
+        const uint8_t *src[2] = {full[0].data(), full[1].data()};
+        pack_pair_tiles(src, 2, F, D, packed);
+        rc = upload(L.pair_hi, packed.data(), packed.size());
+        if (rc == FFNRM_OK) rc = upload_scales(L.beta, beta, F, G, L.scales_half);
+    }
+    if (rc == FFNRM_OK) rc = upload_scales(L.alpha, alpha, F, G, L.scales_half);
+    if (rc == FFNRM_OK && ctx->cfg.max_tokens > ffnrm::kGemvMaxTokens) {
+        const uint8_t *src[2] = {lo[0].data(), lo[1].data()};
+        pack_codes8(src, F, D, packed);
+        rc = upload(L.codes8, packed.data(), packed.size());
+        if (rc == FFNRM_OK &&
+            !make_u8_map(&L.codes8_map, L.codes8.ptr, uint64_t(D), uint64_t((F + 63) / 64 * 128), 128))
+            rc = fail(FFNRM_ERR_CUDA, "cuTensorMapEncodeTiled rejected the byte codes");
     }
     if (rc == FFNRM_OK) rc = upload_down(L.down, w->down, w->down_ld, F, D);
     if (rc == FFNRM_OK && !make_fp16_map(&L.down_map, L.down.ptr, uint64_t((F + 15) / 16 * 16), uint64_t(D),
@@ -850,12 +904,10 @@ int ffnrm_layer_bytes(ffnrm_ctx *ctx, int layer, int64_t *residual_bytes, int64_
     if (rc) return rc;
     const LayerDev &L = ctx->layers[size_t(layer)];
     int64_t res = 0;
-    for (int q = 0; q < 2; ++q) res += int64_t(L.alpha[q].bytes);
+    res += int64_t(L.alpha.bytes);
     const int r = ctx->cfg.residual_bits;
-    for (int q = 0; q < 2; ++q) {
-        if (r != 1) res += int64_t(L.pair[q].bytes);
-        if (r != 2) res += int64_t(L.plane[q].bytes);
-    }
+    if (r != 1) res += int64_t(L.pair.bytes);
+    if (r != 2) res += int64_t(L.plane.bytes);
     if (residual_bytes) *residual_bytes = res;
     if (down_bytes) *down_bytes = int64_t(L.down.bytes);
     return FFNRM_OK;

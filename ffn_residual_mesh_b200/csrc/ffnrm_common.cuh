@@ -1,22 +1,24 @@
 // Shared device-side definitions for the B200 exact base/residual split kernels.
 //
 // Device layouts (chosen at load time; the host converts from the reference's
-// artifact formats). F32 = ceil(F/32) row blocks, C = G/2 chunks of two 32-code
-// groups, "il" = 32 rows interleaved so that lane l of a warp owns row 32*rb + l and
-// one warp-wide load of chunk c reads 32 consecutive 16-byte (or 8-byte) records:
+// artifact formats). C = G/2 chunks of two 32-code groups. Records are tiled by 64-row
+// tiles: for row tile rt and chunk c, the 128 records of the gate rows rt*64..+63 and
+// then the up rows of the same tile are contiguous, so one 32-row block of one
+// projection (a warp's lanes) is 32 consecutive records and one tile's K chunk is a
+// single contiguous run for a bulk copy. A projection's view starts at record 64*proj;
+// rec_index() gives the record of (32-row block rb, chunk c, lane) from there.
 //
-//   pair_il  [F32][C][32][16 B]  bits 0-1 of every code. Word j of a record holds group
-//            2c + (j>>1), codes 16*(j&1) .. +15; code 4i+b of those 16 sits at bit 8b+2i,
-//            so (w >> 2i) & 0x03030303 is the dp4a operand for activations 4i..4i+3 in
-//            natural order.
-//   plane_il [F32][C][32][8 B]   one bit of every code (bit 0 for r = 1, bit 2 for r = 3).
-//            Word j holds group 2c + j; code 4i+b at bit 8b+i, so (w >> i) & 0x01010101
-//            pairs with activations 4i..4i+3.
-//   pair_hi  like pair_il, bits 2-3 (fallback tiles only).
-//   alpha/beta [F32][C][32][2]   fp16 when lossless, else f32.
-//   down_il  [D/32][F/8][32][8 fp16]  the down weight, output row o = 32*ob + lane.
+//   pair  [F64][C][2][64][16 B]  bits 0-1 of every code. Word j of a record holds group
+//         2c + (j>>1), codes 16*(j&1) .. +15; code 4i+b of those 16 sits at bit 8b+2i,
+//         so (w >> 2i) & 0x03030303 is the dp4a operand for activations 4i..4i+3 in
+//         natural order.
+//   plane [F64][C][2][64][8 B]   one bit of every code (bit 0 for r = 1, bit 2 for r = 3).
+//         Word j holds group 2c + j; code 4i+b at bit 8b+i, so (w >> i) & 0x01010101
+//         pairs with activations 4i..4i+3.
+//   pair_hi  like pair, bits 2-3 (fallback tiles only).
+//   alpha/beta [F64][C][2][64][2]   fp16 when lossless, else f32.
 //
-// Rows F..32*F32-1 are zero padding. The residual group dot of row f, group g is
+// Rows F..64*F64-1 are zero padding. The residual group dot of row f, group g is
 //   r = 1: P = dot(plane, z)   r = 2: P = dot(pair, z)   r = 3: P = dot(pair, z) + 4 dot(plane, z)
 // and the unsplit fallback dot is dot(pair, z) + 4 dot(pair_hi, z).
 #pragma once
@@ -28,6 +30,11 @@
 namespace ffnrm {
 
 constexpr int kGroup = 32;
+
+// Record of (32-row block rb, chunk c, lane) relative to a projection's view.
+__host__ __device__ __forceinline__ int64_t rec_index(int rb, int C, int c, int lane) {
+    return (int64_t(rb >> 1) * C + c) * 128 + (rb & 1) * 32 + lane;
+}
 
 struct ProjView {
     const uint4 *pair;

@@ -54,6 +54,7 @@ __device__ __forceinline__ void store_h(const ResidualParams &p, int tok, int ro
 }
 
 constexpr int kResWarps = 4;  // per projection; the CTA runs 2 * kResWarps warps
+constexpr int kGemvMaxTokens = 4;  // larger batches go to the tensor cores
 
 // Shared memory: [z TT*D int8][s TT*G f32][zsum TT*G f32][red 2*kResWarps*TT*32 f32]
 inline size_t residual_smem_bytes(int TT, int D) {
@@ -125,7 +126,7 @@ __global__ void __launch_bounds__(2 * kResWarps * 32, TT == 1 ? 3 : 2) residual_
             wqb[u] = make_uint2(0, 0);
             a0b[u] = a1b[u] = 0.f;
             if (c < c_end) {
-                const int64_t rec = (int64_t(rb) * C + c) * 32 + lane;
+                const int64_t rec = rec_index(rb, C, c, lane);
                 if (RB != 1) wpb[u] = __ldg(pv.pair + rec);
                 if (RB != 2) wqb[u] = __ldg(pv.plane + rec);
                 load_scale2<AHALF>(pv.alpha, rec, a0b[u], a1b[u]);
@@ -140,7 +141,7 @@ __global__ void __launch_bounds__(2 * kResWarps * 32, TT == 1 ? 3 : 2) residual_
             const float a0 = a0b[u], a1 = a1b[u];
             float b0 = 0.f, b1 = 0.f;
             if (flagged) {
-                const int64_t rec = (int64_t(rb) * C + c) * 32 + lane;
+                const int64_t rec = rec_index(rb, C, c, lane);
                 if (RB == 1) wp = __ldg(pv.pair + rec);
                 wh = __ldg(pv.pair_hi + rec);
                 load_scale2<AHALF>(pv.beta, rec, b0, b1);

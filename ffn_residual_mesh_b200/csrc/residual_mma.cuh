@@ -133,15 +133,23 @@ __global__ void __launch_bounds__(128) residual_mma_kernel(const ResidualParams 
             const int slot = i / per_slot, off = (i - slot * per_slot) * 16;
             const int sp = slot >> 1, sb = rb0 + (slot & 1);
             const bool ok = sb < p.row_blocks;
-            const int64_t first = (int64_t(ok ? sb : 0) * C + kc * kMmaChunks) * 32;  // first record
             const ProjView &q = p.proj[sp];
+            // each chunk's 32 records are contiguous; consecutive chunks are a tile apart
             const uint8_t *src;
-            if (off < SL::pair)
-                src = reinterpret_cast<const uint8_t *>(q.pair + first) + off;
-            else if (off < SL::pair + SL::plane)
-                src = reinterpret_cast<const uint8_t *>(q.plane + first) + (off - SL::pair);
-            else
-                src = reinterpret_cast<const uint8_t *>(q.alpha) + first * (AHALF ? 4 : 8) + (off - SL::pair - SL::plane);
+            if (off < SL::pair) {
+                const int cl = off / 512;
+                src = reinterpret_cast<const uint8_t *>(q.pair + rec_index(ok ? sb : 0, C, kc * kMmaChunks + cl, 0)) +
+                      (off - cl * 512);
+            } else if (off < SL::pair + SL::plane) {
+                const int o = off - SL::pair, cl = o / 256;
+                src = reinterpret_cast<const uint8_t *>(q.plane + rec_index(ok ? sb : 0, C, kc * kMmaChunks + cl, 0)) +
+                      (o - cl * 256);
+            } else {
+                constexpr int rb_ = AHALF ? 4 : 8, cb = 32 * rb_;
+                const int o = off - SL::pair - SL::plane, cl = o / cb;
+                src = reinterpret_cast<const uint8_t *>(q.alpha) +
+                      rec_index(ok ? sb : 0, C, kc * kMmaChunks + cl, 0) * rb_ + (o - cl * cb);
+            }
             cp_async16(rec_base + slot * SL::block + off, src, ok);
         }
         cp_async_commit();
@@ -207,7 +215,7 @@ __global__ void __launch_bounds__(128) residual_mma_kernel(const ResidualParams 
                     H[i] = make_uint4(0, 0, 0, 0);
                     b[i][0] = b[i][1] = 0.f;
                     if (FB && any_flag) {
-                        const int64_t grec = (int64_t(rb) * C + c) * 32 + g + 8 * i;
+                        const int64_t grec = rec_index(rb, C, c, g + 8 * i);
                         if (RB == 1) L[i] = __ldg(pv.pair + grec);
                         H[i] = __ldg(pv.pair_hi + grec);
                         load_scale2<AHALF>(pv.beta, grec, b[i][0], b[i][1]);

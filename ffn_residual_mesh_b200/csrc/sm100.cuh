@@ -42,19 +42,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 
 // Waits for the phase of `parity` to complete; after kWaitCycles it records `code` in
 // *err and returns false so the kernel can wind down instead of hanging.
-// The clock is read once per 16 polls.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long start = clock64();
-    while (true) {
-#pragma unroll 1
-        for (int i = 0; i < 16; ++i)
-            if (mbar_try_wait(bar, parity)) return true;
+    while (!mbar_try_wait(bar, parity)) {
         if (clock64() - start > kWaitCycles) {
             if (err) atomicExch(err, code);
             return false;
         }
     }
+    return true;
 }
 
 // 2-D TMA tiled load into shared memory, completing on `bar` (no multicast).
