@@ -457,7 +457,7 @@ int launch_residual_tc_t(ffnrm_ctx *ctx, const LayerDev &L, ffnrm::ResidualParam
     FFNRM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
     p.row_blocks = (p.F + 31) / 32;
     p.err = ctx->err;
-    dim3 grid(unsigned((p.F + ffnrm::kTcTileRows - 1) / ffnrm::kTcTileRows), unsigned((p.T + N - 1) / N));
+    dim3 grid(unsigned((p.T + N - 1) / N), unsigned((p.F + ffnrm::kTcTileRows - 1) / ffnrm::kTcTileRows));
     ProfScope prof(ctx, st, FFNRM_KERNEL_RESIDUAL);
     kern<<<grid, ffnrm::kTcThreads, smem, st>>>(L.codes8_map, zm, p, stages);
     ctx->launches++;
@@ -465,8 +465,8 @@ int launch_residual_tc_t(ffnrm_ctx *ctx, const LayerDev &L, ffnrm::ResidualParam
     return FFNRM_OK;
 }
 
-// T <= 4: dp4a GEMV (HBM-bound); larger batches: tcgen05 kind::i8 tiles on the byte
-// codes, or mma.sync tiles when fallback tiles need the unsplit codes.
+// T <= 4: dp4a GEMV on the 2-bit records (HBM-bound); larger batches: tcgen05 kind::i8
+// tiles on the byte codes, or mma.sync tiles when fallback tiles need the unsplit codes.
 template <int RB>
 int launch_residual_rb(ffnrm_ctx *ctx, const LayerDev &L, ffnrm::ResidualParams &p, bool half, cudaStream_t st) {
     if (p.T == 1) return launch_residual_tt<RB, 1>(ctx, p, half, st);

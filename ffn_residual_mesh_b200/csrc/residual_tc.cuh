@@ -21,14 +21,14 @@
 //              ring (released by the drain). A thread's copies run one after another,
 //              so K tiles are issued in batches with one copy per lane.
 //   warp 1     lane 0 issues 4 x tcgen05.mma per K tile into TMEM buffer it%2 (2 buffers
-//              x 4 groups x N int32 columns), each writing its group's dots afresh.
+//              x 4 groups x N int32 columns), each writing its group's dots P afresh.
 //   warps 2-9  drain: two warps per TMEM lane quadrant (a warp reaches only the lanes of
 //              quadrant warp%4), one tile row per thread, token columns [h*N/2,
 //              (h+1)*N/2) for warp half h.
-// The drain adds 0x4B400000 to each int32 dot P (|P| < 2^22) as an integer, which gives
-// the bit pattern of the float 12582912 + P, and removes 12582912 with one packed
-// float subtract: an exact int-to-float conversion. It then applies alpha[row,g]*s[t,g]
-// with packed multiply / FMA. Padded token columns hold zero
+// The drain converts each exact int32 dot P to float (exact, |P| < 2^24), multiplies by
+// s[t,g] and adds alpha[row,g] times that into the accumulator (packed fp32 pairs, two
+// tokens per instruction; s comes from a per-CTA [G][N] table). Padded token columns
+// hold zero
 // activations and zero scales, so the drain runs without per-token branches. The up
 // rows hand their totals to the gate rows through shared memory; the gate rows merge
 // with the base sums and write h = SiLU(g)*u (fp16 hi + lo). Every mbarrier wait is
@@ -48,13 +48,11 @@ constexpr int kTcKTile = 128;    // codes per K tile (4 groups, 2 record chunks)
 constexpr int kTcThreads = 320;  // producer, MMA, 8 drain warps
 constexpr int kTcDrain = 256;    // drain threads
 constexpr int kTcMaxStages = 8;
-constexpr uint32_t kMagicBits = 0x4B400000u;
-constexpr float kMagic = 12582912.0f;
 
-// Shared memory: [operand ring of `stages`][alpha ring of 2*stages][s: G x N f32]
-// [barriers]. Operand stage: A tile [128][128 B], activation tile [N][128 B] (both
-// 128-byte swizzled). Alpha slot: the K tile's two chunks in HBM order, (chunk cc, tile
-// row m) at cc*128 + m, 2 values each.
+// Shared memory: [operand ring of `stages`][alpha ring of 2*stages][s [G][N] f32]
+// [barriers]. Operand stage: A tile [128][128 B],
+// activation tile [N][128 B] (both 128-byte swizzled). Alpha slot: the K tile's two
+// chunks in HBM order, (chunk cc, tile row m) at cc*128 + m, 2 values each.
 template <int N, bool AHALF>
 struct ResTcCfg {
     static constexpr int a_bytes = 128 * kTcKTile;
@@ -86,7 +84,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *ring = smem;
-    uint8_t *aring = ring + S * Cfg::stage_bytes;                           // [2S] alpha slots
+    uint8_t *aring = ring + S * Cfg::stage_bytes;                                 // [2S] alpha slots
     float *s_sm = reinterpret_cast<float *>(aring + 2 * S * Cfg::alpha_bytes);  // [G][N]
     uint64_t *in_full = reinterpret_cast<uint64_t *>(s_sm + p.G * N);
     uint64_t *in_empty = in_full + kTcMaxStages;
@@ -99,8 +97,8 @@ __global__ void __launch_bounds__(kTcThreads, 2)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = p.G, C = G / 2;
-    const int rt = blockIdx.x;  // 64-row tile of each projection
-    const int t0 = blockIdx.y * N;
+    const int rt = blockIdx.y;  // 64-row tile of each projection (token tiles of a row tile
+    const int t0 = blockIdx.x * N;  // run back to back and share its A tiles through L2)
     const int nkt = p.D / kTcKTile;
     const int nvalid = min(N, p.T - t0);
 
@@ -119,8 +117,8 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     }
     if (warp == 1) sm100::tmem_alloc(tmem_slot, Cfg::tmem_cols);
     for (int i = threadIdx.x; i < G * N; i += blockDim.x) {
-        const int tok = i / G, g = i - tok * G;
-        s_sm[g * N + tok] = t0 + tok < p.T ? p.s[int64_t(t0 + tok) * G + g] : 0.f;
+        const int g = i / N, tok = i - g * N;  // consecutive threads, consecutive tokens
+        s_sm[i] = t0 + tok < p.T ? p.s[int64_t(t0 + tok) * G + g] : 0.f;
     }
     sm100::tc_fence_before();
     __syncthreads();
@@ -217,19 +215,17 @@ __global__ void __launch_bounds__(kTcThreads, 2)
                     for (int j = 0; j < GB; ++j) {
                         const int g = 4 * e + j0 + j;
                         const float2 a2 = make_float2(al[j0 + j], al[j0 + j]);
-                        const float2 m2 = make_float2(-kMagic, -kMagic);
                         const float4 *sg = reinterpret_cast<const float4 *>(s_sm + g * N + cbase);
 #pragma unroll
                         for (int k4 = 0; k4 < NH / 4; ++k4) {
                             const float4 sv = sg[k4];
-                            const float2 x0 = sm100::fadd2(
-                                make_float2(__uint_as_float(r[j][4 * k4] + kMagicBits),
-                                            __uint_as_float(r[j][4 * k4 + 1] + kMagicBits)), m2);
-                            const float2 x1 = sm100::fadd2(
-                                make_float2(__uint_as_float(r[j][4 * k4 + 2] + kMagicBits),
-                                            __uint_as_float(r[j][4 * k4 + 3] + kMagicBits)), m2);
-                            acc[2 * k4] = sm100::ffma2(x0, sm100::fmul2(make_float2(sv.x, sv.y), a2), acc[2 * k4]);
-                            acc[2 * k4 + 1] = sm100::ffma2(x1, sm100::fmul2(make_float2(sv.z, sv.w), a2), acc[2 * k4 + 1]);
+                            const float2 x0 = make_float2(__int2float_rn(int(r[j][4 * k4])), __int2float_rn(int(r[j][4 * k4 + 1])));
+                            const float2 x1 =
+                                make_float2(__int2float_rn(int(r[j][4 * k4 + 2])), __int2float_rn(int(r[j][4 * k4 + 3])));
+                            const float2 u0 = sm100::fmul2(x0, make_float2(sv.x, sv.y));
+                            const float2 u1 = sm100::fmul2(x1, make_float2(sv.z, sv.w));
+                            acc[2 * k4] = sm100::ffma2(a2, u0, acc[2 * k4]);
+                            acc[2 * k4 + 1] = sm100::ffma2(a2, u1, acc[2 * k4 + 1]);
                             if constexpr (DOTS) {
                                 if (row < p.F) {
                                     int32_t *dp = p.dots + int64_t(proj) * p.T * p.F * G;

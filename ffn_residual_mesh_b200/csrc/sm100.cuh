@@ -164,6 +164,24 @@ __device__ __forceinline__ void tmem_st(uint32_t taddr, const uint32_t (&r)[NC])
     if constexpr (NC == 8) tmem_st8(taddr, r); else tmem_st16(taddr, r);
 }
 
+// Copy a 128-lane x 256-bit (8 columns of 32 bits) matrix from shared memory (described
+// by `sdesc`) into TMEM at `taddr`, issued by one thread; ordered before this thread's
+// later tcgen05.mma.
+__device__ __forceinline__ void tmem_cp_128x256b(uint32_t taddr, uint64_t sdesc) {
+    asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;\n" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// Shared-memory matrix descriptor without swizzle: 8-row x 16-byte core matrices, `lbo`
+// bytes between core matrices along the row, `sbo` bytes between 8-row groups.
+__device__ __forceinline__ uint64_t smem_desc_plain(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= uint64_t((addr >> 4) & 0x3FFF);
+    d |= uint64_t((lbo >> 4) & 0x3FFF) << 16;
+    d |= uint64_t((sbo >> 4) & 0x3FFF) << 32;
+    d |= uint64_t(1) << 46;  // descriptor version
+    return d;                // layout type 0: no swizzle
+}
+
 // Make this thread's generic-proxy shared-memory writes visible to the async proxy
 // (tensor core operand reads).
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
