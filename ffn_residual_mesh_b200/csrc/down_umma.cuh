@@ -115,21 +115,24 @@ __global__ void __launch_bounds__(128, 1) down_umma_kernel(const __grid_constant
 
     if (warp == 0) {
         // TMA producer warp. A thread's copies do not overlap one another, so K steps are
-        // issued in batches of max(1, S/2) with one copy per lane (lane 3k + op: W, h hi
-        // or h lo of the batch's k-th step), keeping a whole batch in flight.
-        const int B = S / 2 > 1 ? S / 2 : 1;
-        const int k = lane / 3, op = lane - 3 * (lane / 3);
-        int issued = 0;
-        for (int it0 = 0; it0 < nk; it0 += B) {
+        // issued in batches of max(1, S/2) with one copy per lane (lane 3k + op of the
+        // batch's lane group: W, h hi or h lo of its k-th step), and consecutive batches
+        // use different lane groups, keeping several batches in flight.
+        const int B = S / 2 > 1 ? (S / 2 < 10 ? S / 2 : 10) : 1;
+        const int R = 32 / (3 * B);  // lane groups; consecutive batches use different lanes
+        int issued = 0, batch = 0;
+        for (int it0 = 0; it0 < nk; it0 += B, ++batch) {
             const int nb = min(B, nk - it0);
+            const int l = lane - (batch % R) * 3 * B;  // role within this batch's lane group
+            const int k = l >= 0 ? l / 3 : nb, op = l - 3 * (l / 3);
             const int it = it0 + k, s = it % S;
             bool ok = true;
-            if (k < nb && op == 0) {
+            if (l >= 0 && k < nb && op == 0) {
                 ok = sm100::mbar_wait(empty + s, ((it / S) & 1) ^ 1, p.err, sm100::kErrWaitEmpty);
                 if (ok) sm100::mbar_arrive_expect_tx(full + s, Cfg::stage_bytes);
             }
             if (!__all_sync(0xffffffffu, ok)) break;
-            if (k < nb) {
+            if (l >= 0 && k < nb) {
                 uint8_t *st = tiles + s * Cfg::stage_bytes;
                 const int kx = k0 + it * kUmmaK;
                 const CUtensorMap *map = op == 0 ? &tm_w : op == 1 ? &tm_hi : &tm_lo;

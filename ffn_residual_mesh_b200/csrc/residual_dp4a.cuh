@@ -34,6 +34,21 @@ struct ResidualParams {
     int *err;             // pipeline-wait error word (tensor-core kernel), or null
 };
 
+// h = g/(1+exp(-g))*u for one (token, row) of merged g and u; rows >= F are padding and
+// get zeros. Writes fp16 hi and lo = fp16(h - hi).
+__device__ __forceinline__ void write_h(const ResidualParams &p, int tok, int row, float g, float u) {
+    const int64_t i = int64_t(tok) * p.F16 + row;
+    if (row >= p.F) {
+        p.h_hi[i] = __float2half_rn(0.f);
+        p.h_lo[i] = __float2half_rn(0.f);
+        return;
+    }
+    const float h = g / (1.0f + expf(-g)) * u;
+    const __half hi = __float2half_rn(h);
+    p.h_hi[i] = hi;
+    p.h_lo[i] = __float2half_rn(h - __half2float(hi));
+}
+
 // h = g/(1+exp(-g))*u for one (token, row); flagged rows ignore the base (their g/u
 // already are the unsplit projections). Writes fp16 hi and lo = fp16(h - hi).
 __device__ __forceinline__ void store_h(const ResidualParams &p, int tok, int row, float g, float u, bool flagged) {

@@ -49,7 +49,7 @@ constexpr int kTcThreads = 320;  // producer, MMA, 8 drain warps
 constexpr int kTcDrain = 256;    // drain threads
 constexpr int kTcMaxStages = 8;
 
-// Shared memory: [operand ring of `stages`][alpha ring of 2*stages][s [G][N] f32]
+// Shared memory: [operand ring of `stages`][alpha ring of 2*stages][s [G][N+4] f32]
 // [barriers]. Operand stage: A tile [128][128 B],
 // activation tile [N][128 B] (both 128-byte swizzled). Alpha slot: the K tile's two
 // chunks in HBM order, (chunk cc, tile row m) at cc*128 + m, 2 values each.
@@ -63,9 +63,10 @@ struct ResTcCfg {
     static constexpr int tx_bytes = stage_bytes + alpha_bytes;
     static constexpr int tmem_cols = 8 * N;
     static constexpr int xch_stride = N + 1;  // up totals [64][N+1], aliased on stage 0 at the end
+    static constexpr int s_stride = N + 4;    // padded [G][N] scale table rows (16-byte aligned)
     static_assert(a_bytes >= kTcTileRows * xch_stride * 4, "exchange fits a stage");
     static size_t smem(int G, int stages) {
-        return 1024 + size_t(stages) * (stage_bytes + 2 * alpha_bytes) + size_t(G) * N * 4 + 768;
+        return 1024 + size_t(stages) * (stage_bytes + 2 * alpha_bytes) + size_t(G) * s_stride * 4 + 768;
     }
     // Deepest input ring (2..8 stages) that keeps two CTAs per SM, else two stages.
     static int stages_for(int G) {
@@ -85,8 +86,8 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *ring = smem;
     uint8_t *aring = ring + S * Cfg::stage_bytes;                                 // [2S] alpha slots
-    float *s_sm = reinterpret_cast<float *>(aring + 2 * S * Cfg::alpha_bytes);  // [G][N]
-    uint64_t *in_full = reinterpret_cast<uint64_t *>(s_sm + p.G * N);
+    float *s_sm = reinterpret_cast<float *>(aring + 2 * S * Cfg::alpha_bytes);  // [G][N+4]
+    uint64_t *in_full = reinterpret_cast<uint64_t *>(s_sm + p.G * Cfg::s_stride);
     uint64_t *in_empty = in_full + kTcMaxStages;
     uint64_t *al_empty = in_empty + kTcMaxStages;  // [2S]
     uint64_t *acc_full = al_empty + 2 * kTcMaxStages;
@@ -116,9 +117,23 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         sm100::fence_barrier_init();
     }
     if (warp == 1) sm100::tmem_alloc(tmem_slot, Cfg::tmem_cols);
-    for (int i = threadIdx.x; i < G * N; i += blockDim.x) {
-        const int g = i / N, tok = i - g * N;  // consecutive threads, consecutive tokens
-        s_sm[i] = t0 + tok < p.T ? p.s[int64_t(t0 + tok) * G + g] : 0.f;
+    // Scale table: coalesced reads of each token's G scales, all issued before the stores
+    // (the padded row stride spreads the transposing stores over the banks).
+    {
+        constexpr int kU = 8;
+        for (int i0 = threadIdx.x; i0 < G * N; i0 += kU * blockDim.x) {
+            float v[kU];
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                const int i = i0 + u * blockDim.x, tok = i / G, g = i - tok * G;
+                v[u] = i < G * N && t0 + tok < p.T ? __ldg(p.s + int64_t(t0 + tok) * G + g) : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                const int i = i0 + u * blockDim.x, tok = i / G, g = i - tok * G;
+                if (i < G * N) s_sm[g * Cfg::s_stride + tok] = v[u];
+            }
+        }
     }
     sm100::tc_fence_before();
     __syncthreads();
@@ -136,29 +151,32 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     const uint32_t lane_base = tmem + (uint32_t(32 * q) << 16) + uint32_t(cbase);
 
     if (warp == 0) {
-        // Producer warp: batches of B K tiles; lanes [0, B) load the A tiles and lanes
-        // [B, 2B) the activation tiles in one instruction, then lanes [0, B) the alphas.
+        // Producer warp: batches of B K tiles. Consecutive copies from one thread do not
+        // overlap, so each batch uses its own group of 3B lanes (A tiles, activation
+        // tiles, alphas), rotating through the warp so several batches are in flight.
         constexpr int asz = AHALF ? 2 : 4;
-        const int B = S / 2 > 1 ? (S / 2 < 16 ? S / 2 : 16) : 1;
-        int issued = 0;
-        for (int it0 = 0; it0 < nkt; it0 += B) {
+        const int B = S / 2 > 1 ? (S / 2 < 10 ? S / 2 : 10) : 1;
+        const int R = 32 / (3 * B);  // lane groups
+        int issued = 0, batch = 0;
+        for (int it0 = 0; it0 < nkt; it0 += B, ++batch) {
             const int nb = min(B, nkt - it0);
-            const int k = lane < B ? lane : lane - B;
+            const int l = lane - (batch % R) * 3 * B;  // role within this batch's lane group
+            const int k = l < 0 ? nb : (l < B ? l : (l < 2 * B ? l - B : l - 2 * B));
             const int it = it0 + k, s = it % S, sa = it % (2 * S);
             bool ok = true;
-            if (lane < nb) {
+            if (l >= 0 && l < nb) {
                 ok = sm100::mbar_wait(in_empty + s, ((it / S) & 1) ^ 1, p.err, sm100::kErrWaitEmpty) &&
                      sm100::mbar_wait(al_empty + sa, ((it / (2 * S)) & 1) ^ 1, p.err, sm100::kErrWaitEmpty);
                 if (ok) sm100::mbar_arrive_expect_tx(in_full + s, Cfg::tx_bytes);
             }
             if (!__all_sync(0xffffffffu, ok)) break;
             uint8_t *st = ring + s * Cfg::stage_bytes;
-            if (k < nb && lane < 2 * B) {
-                const bool a = lane < B;
+            if (l >= 0 && l < 2 * B && k < nb) {
+                const bool a = l < B;
                 sm100::tma_load_2d(a ? st : st + Cfg::b_off, a ? &tm_a : &tm_z, it * kTcKTile, a ? rt * 128 : t0,
                                    in_full + s);
             }
-            if (lane < nb) {
+            if (l >= 2 * B && l < 3 * B && k < nb) {
                 const int64_t rec = rec_index(2 * rt, C, 2 * it, 0);  // the tile's first record
                 sm100::bulk_load(aring + sa * Cfg::alpha_bytes,
                                  static_cast<const uint8_t *>(p.proj[0].alpha) + rec * 2 * asz, Cfg::alpha_bytes,
@@ -215,7 +233,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
                     for (int j = 0; j < GB; ++j) {
                         const int g = 4 * e + j0 + j;
                         const float2 a2 = make_float2(al[j0 + j], al[j0 + j]);
-                        const float4 *sg = reinterpret_cast<const float4 *>(s_sm + g * N + cbase);
+                        const float4 *sg = reinterpret_cast<const float4 *>(s_sm + g * Cfg::s_stride + cbase);
 #pragma unroll
                         for (int k4 = 0; k4 < NH / 4; ++k4) {
                             const float4 sv = sg[k4];
@@ -259,13 +277,22 @@ __global__ void __launch_bounds__(kTcThreads, 2)
             const int nt = min(NH, nvalid - cbase);
             if (p.h_hi != nullptr) {
                 if (proj == 0 && row < p.F16) {
+                    // all base sums of this thread's tokens are loaded before any h is stored
+                    float gbs[NH], ubs[NH];
 #pragma unroll
-                    for (int k = 0; k < NH / 2; ++k) {
-                        if (2 * k < nt)
-                            store_h(p, t0 + cbase + 2 * k, row, acc[k].x, xch[m * Cfg::xch_stride + cbase + 2 * k], false);
-                        if (2 * k + 1 < nt)
-                            store_h(p, t0 + cbase + 2 * k + 1, row, acc[k].y,
-                                    xch[m * Cfg::xch_stride + cbase + 2 * k + 1], false);
+                    for (int k = 0; k < NH; ++k) {
+                        const bool v = k < nt && row < p.F;
+                        const int64_t bi = int64_t(t0 + cbase + k) * p.F + row;
+                        gbs[k] = v ? __ldg(p.base[0] + bi) : 0.f;
+                        ubs[k] = v ? __ldg(p.base[1] + bi) : 0.f;
+                    }
+#pragma unroll
+                    for (int k = 0; k < NH; ++k) {
+                        if (k < nt) {
+                            const float gv = (k & 1 ? acc[k / 2].y : acc[k / 2].x) + gbs[k];
+                            const float uv = xch[m * Cfg::xch_stride + cbase + k] + ubs[k];
+                            write_h(p, t0 + cbase + k, row, gv, uv);
+                        }
                     }
                 }
             } else if (row < p.F) {
