@@ -289,6 +289,10 @@ def run_ours(args, cfg, rank, world, local_rank):
 
     res_bytes_layer, down_bytes_layer = mesh.layer_bytes(0)
     D, G = cfg.d_model, cfg.d_model // 32
+    tfile = ROOT / "profiles" / "traffic.json"
+    traffic_table = json.loads(tfile.read_text()) if tfile.exists() else {}
+    pfile = ROOT / "MEASURED_PEAKS.json"
+    peaks_all = json.loads(pfile.read_text()) if pfile.exists() else {}
 
     def alg_bytes(T):
         # residual: codes + alpha, activations and scales, both base sums in, h (fp16 hi + lo) out;
@@ -330,7 +334,14 @@ def run_ours(args, cfg, rank, world, local_rank):
         for k, (ms, n) in pk.items():
             if n:
                 us = 1e3 * ms / n
-                per_batch[str(T)][k] = {"us_per_launch": us, "achieved_gbs": ab[k] / (us * 1e-6) / 1e9}
+                e = {"us_per_launch": us, "achieved_gbs": ab[k] / (us * 1e-6) / 1e9,
+                     "dram_bytes_per_launch": traffic_table.get(f"{k}:{cfg.key}:T{T}")}
+                if k == "residual" and T > 4:
+                    # int8 tensor-core work of the exact group dots: 2 x (2 F) x D x T ops
+                    ops = 2.0 * 2 * F * D * T
+                    e["int8_tops"] = ops / (us * 1e-6) / 1e12
+                    e["int8_frac_of_2x_measured_bf16"] = e["int8_tops"] / (2 * peaks_all.get("bf16_tflops", 1590.0))
+                per_batch[str(T)][k] = e
     if use_graphs:
         g_dev.close()
         g_e2e.close()
@@ -353,10 +364,10 @@ def run_ours(args, cfg, rank, world, local_rank):
             kern[k] = {"ms_total": ms, "launches": n, "achieved_gbs": alg[k] / (ms / 1e3) / 1e9 if ms else None,
                        "us_per_launch": 1e3 * ms / n}
     dom = max(kern, key=lambda k: kern[k]["ms_total"])
-    traffic = None
-    tfile = ROOT / "profiles" / "traffic.json"
-    if tfile.exists():
-        traffic = json.loads(tfile.read_text()).get(f"{dom}:{cfg.key}")
+    # DRAM bytes per launch of the dominant kernel, averaged over the step's batch sizes
+    # (each batch size launches it once per layer) from the per-batch ncu captures
+    per_t = [traffic_table.get(f"{dom}:{cfg.key}:T{T}") for T in cfg.tokens]
+    traffic = sum(per_t) / len(per_t) if all(v is not None for v in per_t) else None
     achieved = kern[dom]["achieved_gbs"]
     roofline = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "peak_source": peak_kind, "traffic": traffic,
