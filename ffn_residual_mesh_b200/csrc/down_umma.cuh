@@ -132,9 +132,18 @@ __global__ void __launch_bounds__(128, 1) down_umma_kernel(const __grid_constant
                 if (ok) sm100::mbar_arrive_expect_tx(full + s, Cfg::stage_bytes);
             }
             if (!__all_sync(0xffffffffu, ok)) break;
-            if (l >= 0 && k < nb) {
-                uint8_t *st = tiles + s * Cfg::stage_bytes;
-                const int kx = k0 + it * kUmmaK;
+            uint8_t *st = tiles + s * Cfg::stage_bytes;
+            const int kx = k0 + it * kUmmaK;
+            if (batch == 0) {
+                // The weight does not depend on the preceding kernel: the first weight tiles
+                // load before the dependency wait, h (its output) only after it.
+                if (l >= 0 && k < nb && op == 0) sm100::tma_load_2d(st, &tm_w, kx, m0, full + s);
+                sm100::grid_dependency_wait();
+                sm100::trigger_dependents();
+                if (l >= 0 && k < nb && op != 0)
+                    sm100::tma_load_2d(st + Cfg::a_bytes + (op - 1) * Cfg::b_bytes, op == 1 ? &tm_hi : &tm_lo, kx, t0,
+                                       full + s);
+            } else if (l >= 0 && k < nb) {
                 const CUtensorMap *map = op == 0 ? &tm_w : op == 1 ? &tm_hi : &tm_lo;
                 uint8_t *dst = op == 0 ? st : st + Cfg::a_bytes + (op - 1) * Cfg::b_bytes;
                 sm100::tma_load_2d(dst, map, kx, op == 0 ? m0 : t0, full + s);
@@ -145,7 +154,13 @@ __global__ void __launch_bounds__(128, 1) down_umma_kernel(const __grid_constant
         if (lane == 0)
             for (int it = max(0, issued - S); it < issued; ++it)
                 sm100::mbar_wait(full + it % S, (it / S) & 1, p.err, sm100::kErrWaitFull);
-    } else if (warp == 1 && lane == 0) {
+    } else {
+        // The other warps read only what the producer staged; their y writes wait for the
+        // preceding kernel like every access to its memory (dependent launch).
+        sm100::grid_dependency_wait();
+        sm100::trigger_dependents();
+    }
+    if (warp == 1 && lane == 0) {
         // MMA issuer
         constexpr uint32_t idesc = sm100::umma_idesc_f16_f32(kUmmaM, N);
         for (int it = 0; it < nk; ++it) {

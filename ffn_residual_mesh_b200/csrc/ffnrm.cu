@@ -18,6 +18,7 @@
 #include <mutex>
 #include <new>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "down_umma.cuh"
@@ -110,6 +111,39 @@ bool make_z_map(CUtensorMap *map, const void *z, uint64_t d_model, uint64_t toke
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(z), dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Launches `kern`, when `dependent`, as a programmatic dependent of the preceding kernel of
+// the stream (its launch overlaps that kernel's tail; the kernel waits for it with
+// griddepcontrol.wait before touching its outputs), optionally as clusters of `cluster_x`
+// CTAs along x. The residual kernels launch as dependents; the down projection's clusters
+// do not (launched early they wait on SM space held by the residual and measured slower),
+// but it triggers its dependents so the next residual launch overlaps its tail.
+template <typename... Params, typename... Args>
+cudaError_t launch_dependent(void (*kern)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                             bool dependent, unsigned cluster_x, Args &&...args) {
+    cudaLaunchConfig_t lc{};
+    lc.gridDim = grid;
+    lc.blockDim = block;
+    lc.dynamicSmemBytes = smem;
+    lc.stream = st;
+    cudaLaunchAttribute attr[2];
+    unsigned n = 0;
+    if (dependent) {
+        attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n].val.programmaticStreamSerializationAllowed = 1;
+        ++n;
+    }
+    if (cluster_x > 1) {
+        attr[n].id = cudaLaunchAttributeClusterDimension;
+        attr[n].val.clusterDim.x = cluster_x;
+        attr[n].val.clusterDim.y = 1;
+        attr[n].val.clusterDim.z = 1;
+        ++n;
+    }
+    lc.attrs = attr;
+    lc.numAttrs = n;
+    return cudaLaunchKernelEx(&lc, kern, std::forward<Args>(args)...);
 }
 
 }  // namespace
@@ -412,9 +446,8 @@ int launch_residual_t(ffnrm_ctx *ctx, ffnrm::ResidualParams &p, cudaStream_t st)
     p.row_blocks = (p.F + 31) / 32;
     dim3 grid(unsigned(p.row_blocks), unsigned((p.T + TT - 1) / TT));
     ProfScope prof(ctx, st, FFNRM_KERNEL_RESIDUAL);
-    kern<<<grid, 2 * ffnrm::kResWarps * 32, smem, st>>>(p);
+    FFNRM_CUDA(launch_dependent(kern, grid, dim3(2 * ffnrm::kResWarps * 32), smem, st, true, 1, p));
     ctx->launches++;
-    FFNRM_CUDA(cudaGetLastError());
     return FFNRM_OK;
 }
 
@@ -459,9 +492,8 @@ int launch_residual_tc_t(ffnrm_ctx *ctx, const LayerDev &L, ffnrm::ResidualParam
     p.err = ctx->err;
     dim3 grid(unsigned((p.T + N - 1) / N), unsigned((p.F + ffnrm::kTcTileRows - 1) / ffnrm::kTcTileRows));
     ProfScope prof(ctx, st, FFNRM_KERNEL_RESIDUAL);
-    kern<<<grid, ffnrm::kTcThreads, smem, st>>>(L.codes8_map, zm, p, stages);
+    FFNRM_CUDA(launch_dependent(kern, grid, dim3(ffnrm::kTcThreads), smem, st, true, 1, L.codes8_map, zm, p, stages));
     ctx->launches++;
-    FFNRM_CUDA(cudaGetLastError());
     return FFNRM_OK;
 }
 
@@ -541,19 +573,8 @@ int launch_down_cluster(const CUtensorMap &wm, const CUtensorMap &hm, const CUte
     splits = (ksteps + kc_steps - 1) / kc_steps;
     p.splits = splits;
     p.kc = kc_steps * ffnrm::kUmmaK;
-    cudaLaunchConfig_t lc{};
-    lc.gridDim = dim3(unsigned(splits), unsigned(mt), unsigned(ntile));
-    lc.blockDim = dim3(128, 1, 1);
-    lc.dynamicSmemBytes = Cfg::smem;
-    lc.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = unsigned(splits);
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    lc.attrs = attr;
-    lc.numAttrs = 1;
-    FFNRM_CUDA(cudaLaunchKernelEx(&lc, kern, wm, hm, lm, p));
+    FFNRM_CUDA(launch_dependent(kern, dim3(unsigned(splits), unsigned(mt), unsigned(ntile)), dim3(128), Cfg::smem, st,
+                                false, unsigned(splits), wm, hm, lm, p));
     return FFNRM_OK;
 }
 

@@ -88,6 +88,9 @@ __global__ void __launch_bounds__(2 * kResWarps * 32, TT == 1 ? 3 : 2) residual_
 
     const int rb = blockIdx.x;
     const int t0 = blockIdx.y * TT;
+    // The inputs may come from the preceding kernel of the stream (dependent launch).
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 
     // Stage TT tokens of activations (16-byte copies) and their group scales.
     const int zvec = TT * D / 16;

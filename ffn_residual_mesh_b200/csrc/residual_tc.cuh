@@ -117,6 +117,10 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         sm100::fence_barrier_init();
     }
     if (warp == 1) sm100::tmem_alloc(tmem_slot, Cfg::tmem_cols);
+    // Everything above touches only this CTA's shared memory and TMEM; the inputs may come
+    // from the preceding kernel of the stream (dependent launch).
+    sm100::grid_dependency_wait();
+    sm100::trigger_dependents();
     // Scale table: coalesced reads of each token's G scales, all issued before the stores
     // (the padded row stride spreads the transposing stores over the banks).
     {

@@ -54,6 +54,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
     return true;
 }
 
+// Programmatic dependent launch. grid_dependency_wait() blocks until the preceding
+// kernel of the stream has completed and its memory is visible (a no-op when the kernel
+// was not launched as a dependent); trigger_dependents() lets the next kernel of the
+// stream start launching once every CTA of this grid has executed it or exited.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void trigger_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+
 // 2-D TMA tiled load into shared memory, completing on `bar` (no multicast).
 __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
     asm volatile(
