@@ -246,7 +246,10 @@ def run_ours(args, cfg, rank, world, local_rank):
             dist.barrier()
         return ms
 
-    use_graphs = world == 1 and not args.eager
+    # NCCL collectives are captured with the kernels (all ranks capture the same calls, after
+    # an eager warm-up has created the communicators); graphs are released before the process
+    # group is destroyed.
+    use_graphs = not args.eager
     launches0 = mesh.launches
     step_device()
     torch.cuda.synchronize()
