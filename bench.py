@@ -315,6 +315,16 @@ def run_ours(args, cfg, rank, world, local_rank):
                              "us_per_layer": 1e3 * ms_b / args.steps / cfg.layers}
         if runner:
             runner.close()
+
+        def one_batch_e2e(T=T):
+            for l in range(cfg.layers):
+                h = inputs[(T, l)]["host"]
+                stack.forward_host(l, h["z"], h["s"], h["gb"], h["ub"], h["y16"], staging=staging)
+        runner = StepGraph(one_batch_e2e) if use_graphs else None
+        ms_e = timed(runner.replay if runner else one_batch_e2e, args.steps)
+        per_batch[str(T)]["e2e_us_per_layer"] = 1e3 * ms_e / args.steps / cfg.layers
+        if runner:
+            runner.close()
         # per-kernel device time for this batch size alone
         mesh.profile(True)
         pk = {"residual": [0.0, 0], "down": [0.0, 0]}

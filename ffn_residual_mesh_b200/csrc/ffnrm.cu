@@ -440,7 +440,7 @@ struct ProfScope {
 // ---------------------------------------------------------------------------
 template <int RB, int TT, bool AH>
 int launch_residual_t(ffnrm_ctx *ctx, ffnrm::ResidualParams &p, cudaStream_t st) {
-    const size_t smem = ffnrm::residual_smem_bytes(TT, p.D);
+    const size_t smem = ffnrm::residual_smem_bytes<RB, AH>(TT, p.D);
     auto kern = ffnrm::residual_gemv_kernel<RB, TT, AH>;
     if (smem > 48 * 1024) FFNRM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
     p.row_blocks = (p.F + 31) / 32;

@@ -31,6 +31,23 @@ namespace ffnrm {
 
 constexpr int kGroup = 32;
 
+// Asynchronous global -> shared copies (cp.async). The 16-byte form zero-fills when
+// `valid` is false.
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gmem_src, bool valid) {
+    const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
+    const int bytes = valid ? 16 : 0;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(gmem_src), "r"(bytes));
+}
+template <int BYTES>
+__device__ __forceinline__ void cp_async_small(void *smem_dst, const void *gmem_src) {
+    static_assert(BYTES == 4 || BYTES == 8, "4 or 8 bytes");
+    const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], %2;\n" ::"r"(dst), "l"(gmem_src), "n"(BYTES));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
 // Record of (32-row block rb, chunk c, lane) relative to a projection's view.
 __host__ __device__ __forceinline__ int64_t rec_index(int rb, int C, int c, int lane) {
     return (int64_t(rb >> 1) * C + c) * 128 + (rb & 1) * 32 + lane;

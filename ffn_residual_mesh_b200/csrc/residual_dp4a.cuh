@@ -71,20 +71,38 @@ __device__ __forceinline__ void store_h(const ResidualParams &p, int tok, int ro
 constexpr int kResWarps = 4;  // per projection; the CTA runs 2 * kResWarps warps
 constexpr int kGemvMaxTokens = 4;  // larger batches go to the tensor cores
 
+// Each warp streams its chunk records through a cp.async ring of kGemvBufs windows of
+// kGemvWin chunks, so about kGemvBufs * kGemvWin chunks per lane are in flight while it
+// computes.
+constexpr int kGemvWin = 4, kGemvBufs = 3;
+template <int RB, bool AHALF>
+struct GemvStage {
+    static constexpr int pair = RB != 1 ? 16 : 0;  // bytes per lane and chunk
+    static constexpr int plane = RB != 2 ? 8 : 0;
+    static constexpr int alpha = AHALF ? 4 : 8;
+    static constexpr int warp_bytes = kGemvBufs * kGemvWin * 32 * (pair + plane + alpha);
+};
+
 // Shared memory: [z TT*D int8][s TT*G f32][zsum TT*G f32][red 2*kResWarps*TT*32 f32]
+// [per-warp record rings]
+template <int RB, bool AHALF>
 inline size_t residual_smem_bytes(int TT, int D) {
     const int G = D / 32;
-    return size_t(TT) * D + size_t(TT) * G * 8 + size_t(2 * kResWarps) * TT * 32 * 4;
+    const size_t head = size_t(TT) * D + size_t(TT) * G * 8 + size_t(2 * kResWarps) * TT * 32 * 4;
+    return (head + 15) / 16 * 16 + size_t(2 * kResWarps) * GemvStage<RB, AHALF>::warp_bytes;
 }
 
 template <int RB, int TT, bool AHALF>
 __global__ void __launch_bounds__(2 * kResWarps * 32, TT == 1 ? 3 : 2) residual_gemv_kernel(const ResidualParams p) {
+    using GS = GemvStage<RB, AHALF>;
     extern __shared__ __align__(16) uint8_t smem[];
     const int G = p.G, D = p.D, F = p.F, T = p.T;
     int8_t *z_sm = reinterpret_cast<int8_t *>(smem);
     float *s_sm = reinterpret_cast<float *>(smem + size_t(TT) * D);
     float *zsum_sm = s_sm + TT * G;
     float *red = zsum_sm + TT * G;
+    const size_t head = size_t(TT) * D + size_t(TT) * G * 8 + size_t(2 * kResWarps) * TT * 32 * 4;
+    uint8_t *rings = smem + (head + 15) / 16 * 16;
 
     const int rb = blockIdx.x;
     const int t0 = blockIdx.y * TT;
@@ -130,33 +148,46 @@ __global__ void __launch_bounds__(2 * kResWarps * 32, TT == 1 ? 3 : 2) residual_
 #pragma unroll
     for (int t = 0; t < TT; ++t) acc[t] = 0.f;
 
-    // Loads of kBatch chunks are issued together before any is used (kBatch x 20 bytes
-    // per lane in flight); the rare fallback rows load their extra data when used.
-    constexpr int kBatch = 4;
-    for (int cb = c_begin; cb < c_end; cb += kBatch) {
-        uint4 wpb[kBatch];
-        uint2 wqb[kBatch];
-        float a0b[kBatch], a1b[kBatch];
+    // The warp's chunk records stream through its cp.async ring; each lane reads back only
+    // what it copied. The rare fallback rows load their extra data when used.
+    uint8_t *ring = rings + size_t(warp) * GS::warp_bytes;
+    uint4 *pair_r = reinterpret_cast<uint4 *>(ring);                                          // [bufs][win][32]
+    uint2 *plane_r = reinterpret_cast<uint2 *>(ring + kGemvBufs * kGemvWin * 32 * GS::pair);  // [bufs][win][32]
+    uint8_t *alpha_r = ring + kGemvBufs * kGemvWin * 32 * (GS::pair + GS::plane);             // [bufs][win][32]
+    const int nwin = (c_end - c_begin + kGemvWin - 1) / kGemvWin;
+    auto issue = [&](int w) {  // window w into buffer w % kGemvBufs (an empty group past the end)
+        if (w < nwin) {
+            const int b = w % kGemvBufs;
 #pragma unroll
-        for (int u = 0; u < kBatch; ++u) {
-            const int c = cb + u;
-            wpb[u] = make_uint4(0, 0, 0, 0);
-            wqb[u] = make_uint2(0, 0);
-            a0b[u] = a1b[u] = 0.f;
-            if (c < c_end) {
-                const int64_t rec = rec_index(rb, C, c, lane);
-                if (RB != 1) wpb[u] = __ldg(pv.pair + rec);
-                if (RB != 2) wqb[u] = __ldg(pv.plane + rec);
-                load_scale2<AHALF>(pv.alpha, rec, a0b[u], a1b[u]);
+            for (int u = 0; u < kGemvWin; ++u) {
+                const int c = c_begin + w * kGemvWin + u;
+                if (c < c_end) {
+                    const int64_t rec = rec_index(rb, C, c, lane);
+                    const int slot = (b * kGemvWin + u) * 32 + lane;
+                    if (RB != 1) cp_async16(pair_r + slot, pv.pair + rec, true);
+                    if (RB != 2) cp_async_small<8>(plane_r + slot, pv.plane + rec);
+                    cp_async_small<GS::alpha>(alpha_r + size_t(slot) * GS::alpha,
+                                              static_cast<const uint8_t *>(pv.alpha) + rec * GS::alpha);
+                }
             }
         }
+        cp_async_commit();
+    };
 #pragma unroll
-        for (int u = 0; u < kBatch; ++u) {
-            const int c = cb + u;
+    for (int w = 0; w < kGemvBufs - 1; ++w) issue(w);
+    for (int w = 0; w < nwin; ++w) {
+        issue(w + kGemvBufs - 1);
+        cp_async_wait<kGemvBufs - 1>();  // window w has landed
+        const int b = w % kGemvBufs;
+#pragma unroll
+        for (int u = 0; u < kGemvWin; ++u) {
+            const int c = c_begin + w * kGemvWin + u;
             if (c >= c_end) break;
-            uint4 wp = wpb[u], wh = make_uint4(0, 0, 0, 0);
-            const uint2 wq = wqb[u];
-            const float a0 = a0b[u], a1 = a1b[u];
+            const int slot = (b * kGemvWin + u) * 32 + lane;
+            uint4 wp = RB != 1 ? pair_r[slot] : make_uint4(0, 0, 0, 0), wh = make_uint4(0, 0, 0, 0);
+            const uint2 wq = RB != 2 ? plane_r[slot] : make_uint2(0, 0);
+            float a0, a1;
+            load_scale2_shared<AHALF>(alpha_r, slot, a0, a1);
             float b0 = 0.f, b1 = 0.f;
             if (flagged) {
                 const int64_t rec = rec_index(rb, C, c, lane);
@@ -196,6 +227,7 @@ __global__ void __launch_bounds__(2 * kResWarps * 32, TT == 1 ? 3 : 2) residual_
             }
         }
     }
+    cp_async_wait<0>();
 #pragma unroll
     for (int t = 0; t < TT; ++t) red[(warp * TT + t) * 32 + lane] = acc[t];
     __syncthreads();

@@ -35,15 +35,6 @@ __device__ __forceinline__ void mma_u8s8(int (&d)[4], const uint32_t (&a)[4], ui
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 
-__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gmem_src, bool valid) {
-    const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
-    const int bytes = valid ? 16 : 0;  // zero-fill when the source is past the data
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(gmem_src), "r"(bytes));
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
-
 // Codes 4t..4t+3 (k0) and 16+4t..16+4t+3 (k1) of one row and group as u8 bytes.
 template <int RB>
 __device__ __forceinline__ void group_codes(uint32_t lo, uint32_t hi, uint32_t plane, int t, uint32_t &k0,
