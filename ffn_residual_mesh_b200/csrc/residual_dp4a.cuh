@@ -106,7 +106,43 @@ __global__ void __launch_bounds__(2 * kResWarps * 32, TT == 1 ? 3 : 2) residual_
 
     const int rb = blockIdx.x;
     const int t0 = blockIdx.y * TT;
-    // The inputs may come from the preceding kernel of the stream (dependent launch).
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int proj = warp / kResWarps, wk = warp - proj * kResWarps;
+    const int row = rb * 32 + lane;
+    const bool valid = row < F;
+    const ProjView pv = p.proj[proj];
+    const int C = G / 2;
+    const int c_begin = wk * C / kResWarps, c_end = (wk + 1) * C / kResWarps;
+
+    // The warp's chunk records stream through its cp.async ring; each lane reads back only
+    // what it copied. The rare fallback rows load their extra data when used. The records
+    // and alphas are weights, so the first windows go out before the wait on the preceding
+    // kernel of the stream (dependent launch); activations, scales and flags after it.
+    uint8_t *ring = rings + size_t(warp) * GS::warp_bytes;
+    uint4 *pair_r = reinterpret_cast<uint4 *>(ring);                                          // [bufs][win][32]
+    uint2 *plane_r = reinterpret_cast<uint2 *>(ring + kGemvBufs * kGemvWin * 32 * GS::pair);  // [bufs][win][32]
+    uint8_t *alpha_r = ring + kGemvBufs * kGemvWin * 32 * (GS::pair + GS::plane);             // [bufs][win][32]
+    const int nwin = (c_end - c_begin + kGemvWin - 1) / kGemvWin;
+    auto issue = [&](int w) {  // window w into buffer w % kGemvBufs (an empty group past the end)
+        if (w < nwin) {
+            const int b = w % kGemvBufs;
+#pragma unroll
+            for (int u = 0; u < kGemvWin; ++u) {
+                const int c = c_begin + w * kGemvWin + u;
+                if (c < c_end) {
+                    const int64_t rec = rec_index(rb, C, c, lane);
+                    const int slot = (b * kGemvWin + u) * 32 + lane;
+                    if (RB != 1) cp_async16(pair_r + slot, pv.pair + rec, true);
+                    if (RB != 2) cp_async_small<8>(plane_r + slot, pv.plane + rec);
+                    cp_async_small<GS::alpha>(alpha_r + size_t(slot) * GS::alpha,
+                                              static_cast<const uint8_t *>(pv.alpha) + rec * GS::alpha);
+                }
+            }
+        }
+        cp_async_commit();
+    };
+#pragma unroll
+    for (int w = 0; w < kGemvBufs - 1; ++w) issue(w);
     asm volatile("griddepcontrol.wait;\n" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 
@@ -135,46 +171,11 @@ __global__ void __launch_bounds__(2 * kResWarps * 32, TT == 1 ? 3 : 2) residual_
     }
     __syncthreads();
 
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int proj = warp / kResWarps, wk = warp - proj * kResWarps;
-    const int row = rb * 32 + lane;
-    const bool valid = row < F;
     const bool flagged = valid && row_flagged(p.fallback_tiles, row, p.tile_rows);
-    const ProjView pv = p.proj[proj];
-    const int C = G / 2;
-    const int c_begin = wk * C / kResWarps, c_end = (wk + 1) * C / kResWarps;
-
     float acc[TT];
 #pragma unroll
     for (int t = 0; t < TT; ++t) acc[t] = 0.f;
 
-    // The warp's chunk records stream through its cp.async ring; each lane reads back only
-    // what it copied. The rare fallback rows load their extra data when used.
-    uint8_t *ring = rings + size_t(warp) * GS::warp_bytes;
-    uint4 *pair_r = reinterpret_cast<uint4 *>(ring);                                          // [bufs][win][32]
-    uint2 *plane_r = reinterpret_cast<uint2 *>(ring + kGemvBufs * kGemvWin * 32 * GS::pair);  // [bufs][win][32]
-    uint8_t *alpha_r = ring + kGemvBufs * kGemvWin * 32 * (GS::pair + GS::plane);             // [bufs][win][32]
-    const int nwin = (c_end - c_begin + kGemvWin - 1) / kGemvWin;
-    auto issue = [&](int w) {  // window w into buffer w % kGemvBufs (an empty group past the end)
-        if (w < nwin) {
-            const int b = w % kGemvBufs;
-#pragma unroll
-            for (int u = 0; u < kGemvWin; ++u) {
-                const int c = c_begin + w * kGemvWin + u;
-                if (c < c_end) {
-                    const int64_t rec = rec_index(rb, C, c, lane);
-                    const int slot = (b * kGemvWin + u) * 32 + lane;
-                    if (RB != 1) cp_async16(pair_r + slot, pv.pair + rec, true);
-                    if (RB != 2) cp_async_small<8>(plane_r + slot, pv.plane + rec);
-                    cp_async_small<GS::alpha>(alpha_r + size_t(slot) * GS::alpha,
-                                              static_cast<const uint8_t *>(pv.alpha) + rec * GS::alpha);
-                }
-            }
-        }
-        cp_async_commit();
-    };
-#pragma unroll
-    for (int w = 0; w < kGemvBufs - 1; ++w) issue(w);
     for (int w = 0; w < nwin; ++w) {
         issue(w + kGemvBufs - 1);
         cp_async_wait<kGemvBufs - 1>();  // window w has landed

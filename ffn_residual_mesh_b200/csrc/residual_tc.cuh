@@ -117,28 +117,11 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         sm100::fence_barrier_init();
     }
     if (warp == 1) sm100::tmem_alloc(tmem_slot, Cfg::tmem_cols);
-    // Everything above touches only this CTA's shared memory and TMEM; the inputs may come
-    // from the preceding kernel of the stream (dependent launch).
-    sm100::grid_dependency_wait();
+    // Everything up to the role split touches only this CTA's shared memory and TMEM. The
+    // activations, scales and base sums may come from the preceding kernel of the stream
+    // (dependent launch): the producer waits for it after its first weight copies, the
+    // drain before it reads anything.
     sm100::trigger_dependents();
-    // Scale table: coalesced reads of each token's G scales, all issued before the stores
-    // (the padded row stride spreads the transposing stores over the banks).
-    {
-        constexpr int kU = 8;
-        for (int i0 = threadIdx.x; i0 < G * N; i0 += kU * blockDim.x) {
-            float v[kU];
-#pragma unroll
-            for (int u = 0; u < kU; ++u) {
-                const int i = i0 + u * blockDim.x, tok = i / G, g = i - tok * G;
-                v[u] = i < G * N && t0 + tok < p.T ? __ldg(p.s + int64_t(t0 + tok) * G + g) : 0.f;
-            }
-#pragma unroll
-            for (int u = 0; u < kU; ++u) {
-                const int i = i0 + u * blockDim.x, tok = i / G, g = i - tok * G;
-                if (i < G * N) s_sm[g * Cfg::s_stride + tok] = v[u];
-            }
-        }
-    }
     sm100::tc_fence_before();
     __syncthreads();
     sm100::tc_fence_after();
@@ -175,17 +158,16 @@ __global__ void __launch_bounds__(kTcThreads, 2)
             }
             if (!__all_sync(0xffffffffu, ok)) break;
             uint8_t *st = ring + s * Cfg::stage_bytes;
-            if (l >= 0 && l < 2 * B && k < nb) {
-                const bool a = l < B;
-                sm100::tma_load_2d(a ? st : st + Cfg::b_off, a ? &tm_a : &tm_z, it * kTcKTile, a ? rt * 128 : t0,
-                                   in_full + s);
-            }
+            if (l >= 0 && l < B && k < nb) sm100::tma_load_2d(st, &tm_a, it * kTcKTile, rt * 128, in_full + s);
             if (l >= 2 * B && l < 3 * B && k < nb) {
                 const int64_t rec = rec_index(2 * rt, C, 2 * it, 0);  // the tile's first record
                 sm100::bulk_load(aring + sa * Cfg::alpha_bytes,
                                  static_cast<const uint8_t *>(p.proj[0].alpha) + rec * 2 * asz, Cfg::alpha_bytes,
                                  in_full + s);
             }
+            // codes and alpha are weights; the activations follow the preceding kernel
+            if (batch == 0) sm100::grid_dependency_wait();
+            if (l >= B && l < 2 * B && k < nb) sm100::tma_load_2d(st + Cfg::b_off, &tm_z, it * kTcKTile, t0, in_full + s);
             issued = it0 + nb;
         }
         // No copy may still be in flight when the CTA exits.
@@ -211,7 +193,28 @@ __global__ void __launch_bounds__(kTcThreads, 2)
             sm100::umma_commit(done);
         }
     } else {
-        // Drain.
+        // Drain. Scale table first: coalesced reads of each token's G scales, all issued
+        // before the stores (the padded row stride spreads the transposing stores over
+        // the banks).
+        sm100::grid_dependency_wait();
+        {
+            constexpr int kU = 8;
+            const int dt = threadIdx.x - 64;
+            for (int i0 = dt; i0 < G * N; i0 += kU * kTcDrain) {
+                float v[kU];
+#pragma unroll
+                for (int u = 0; u < kU; ++u) {
+                    const int i = i0 + u * kTcDrain, tok = i / G, g = i - tok * G;
+                    v[u] = i < G * N && t0 + tok < p.T ? __ldg(p.s + int64_t(t0 + tok) * G + g) : 0.f;
+                }
+#pragma unroll
+                for (int u = 0; u < kU; ++u) {
+                    const int i = i0 + u * kTcDrain, tok = i / G, g = i - tok * G;
+                    if (i < G * N) s_sm[g * Cfg::s_stride + tok] = v[u];
+                }
+            }
+            asm volatile("bar.sync 1, %0;\n" ::"r"(kTcDrain) : "memory");
+        }
         float2 acc[NH / 2];
 #pragma unroll
         for (int k = 0; k < NH / 2; ++k) acc[k] = make_float2(0.f, 0.f);
