@@ -15,6 +15,7 @@ LIB_PATH = Path(__file__).resolve().parent / "lib" / "libffnrm.so"
 OK, ERR_ARG, ERR_CUDA, ERR_STATE, ERR_NOMEM, ERR_TIMEOUT = 0, 1, 2, 3, 4, 5
 CODES_Q4_BYTES, CODES_QLO2_ROWPACKED, CODES_BITPLANES = 0, 1, 2
 KERNEL_RESIDUAL, KERNEL_DOWN, KERNEL_REDUCE = 0, 1, 2
+IPC_HANDLE_BYTES = 64
 
 # Every symbol include/ffnrm.h declares, with its ctypes signature.
 SIGNATURES = {
@@ -30,6 +31,11 @@ SIGNATURES = {
     "ffnrm_host_register": (c_int, [c_void_p, c_size_t]),
     "ffnrm_host_unregister": (c_int, [c_void_p]),
     "ffnrm_cast_f16": (c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
+    "ffnrm_peer_create": (c_int, [POINTER(c_void_p), c_int, c_int, c_int, c_int64, c_void_p]),
+    "ffnrm_peer_connect": (c_int, [c_void_p, c_void_p]),
+    "ffnrm_peer_allreduce": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p]),
+    "ffnrm_peer_check": (c_int, [c_void_p, c_void_p]),
+    "ffnrm_peer_destroy": (c_int, [c_void_p]),
     "ffnrm_layer_bytes": (c_int, [c_void_p, c_int, POINTER(c_int64), POINTER(c_int64)]),
     "ffnrm_launch_count": (c_int64, [c_void_p]),
     "ffnrm_check_device_error": (c_int, [c_void_p, c_void_p]),

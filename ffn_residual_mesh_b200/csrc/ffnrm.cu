@@ -25,6 +25,7 @@
 #include "ffnrm_common.cuh"
 #include "residual_dp4a.cuh"
 #include "residual_mma.cuh"
+#include "peer_reduce.cuh"
 #include "residual_tc.cuh"
 
 namespace {
@@ -917,6 +918,136 @@ int ffnrm_cast_f16(const float *src, uint16_t *dst, int64_t n, void *stream) {
     const int blocks = int(std::min<int64_t>((n + 255) / 256, 1024));
     ffnrm::cast_f16_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(src, reinterpret_cast<__half *>(dst), n);
     FFNRM_CUDA(cudaGetLastError());
+    return FFNRM_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Peer reduction of the sharded stack's layer output (NVLink, CUDA IPC)
+// ---------------------------------------------------------------------------
+struct ffnrm_peer {
+    int device = 0, world = 1, rank = 0;
+    int64_t max_elems = 0;
+    void *region = nullptr;  // receive slots [2][world][max_elems] f32, then flags [world][chunks] u32
+    size_t recv_bytes = 0, region_bytes = 0;
+    void *mapped[ffnrm::kPeerMaxRanks] = {};  // peers' regions opened here (own: region)
+    uint32_t *counters = nullptr;              // epoch, done
+    int *status = nullptr;
+    bool connected = false;
+};
+
+int ffnrm_peer_create(ffnrm_peer **out, int device, int world, int rank, int64_t max_elems, void *ipc_handle) {
+    if (!out || !ipc_handle) return fail(FFNRM_ERR_ARG, "null argument");
+    *out = nullptr;
+    if (world < 2 || world > ffnrm::kPeerMaxRanks || rank < 0 || rank >= world)
+        return fail(FFNRM_ERR_ARG, "world=%d rank=%d: 2..%d ranks", world, rank, ffnrm::kPeerMaxRanks);
+    if (max_elems <= 0 || max_elems % 4)
+        return fail(FFNRM_ERR_ARG, "max_elems=%lld must be a positive multiple of 4", (long long)max_elems);
+    DeviceGuard guard(device);
+    auto *pr = new (std::nothrow) ffnrm_peer;
+    if (!pr) return fail(FFNRM_ERR_NOMEM, "host allocation failed");
+    pr->device = device;
+    pr->world = world;
+    pr->rank = rank;
+    pr->max_elems = max_elems;
+    pr->recv_bytes = size_t(2) * world * size_t(max_elems) * 4;
+    pr->region_bytes = pr->recv_bytes + size_t(world) * ffnrm::kPeerMaxChunks * 4;
+    cudaIpcMemHandle_t h;
+    const bool ok = cudaMalloc(&pr->region, pr->region_bytes) == cudaSuccess &&
+                    cudaMemset(pr->region, 0, pr->region_bytes) == cudaSuccess &&
+                    cudaMalloc(&pr->counters, 2 * sizeof(uint32_t)) == cudaSuccess &&
+                    cudaMemset(pr->counters, 0, 2 * sizeof(uint32_t)) == cudaSuccess &&
+                    cudaMalloc(&pr->status, sizeof(int)) == cudaSuccess &&
+                    cudaMemset(pr->status, 0, sizeof(int)) == cudaSuccess &&
+                    cudaIpcGetMemHandle(&h, pr->region) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
+    if (!ok) {
+        const cudaError_t e = cudaGetLastError();
+        ffnrm_peer_destroy(pr);
+        return fail(FFNRM_ERR_CUDA, "peer region set-up failed: %s", cudaGetErrorString(e));
+    }
+    std::memcpy(ipc_handle, &h, sizeof(h));
+    pr->mapped[rank] = pr->region;
+    *out = pr;
+    return FFNRM_OK;
+}
+
+int ffnrm_peer_connect(ffnrm_peer *pr, const void *ipc_handles) {
+    if (!pr || !ipc_handles) return fail(FFNRM_ERR_ARG, "null argument");
+    if (pr->connected) return fail(FFNRM_ERR_STATE, "already connected");
+    DeviceGuard guard(pr->device);
+    for (int k = 0; k < pr->world; ++k) {
+        if (k == pr->rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, static_cast<const uint8_t *>(ipc_handles) + size_t(k) * sizeof(h), sizeof(h));
+        const cudaError_t e = cudaIpcOpenMemHandle(&pr->mapped[k], h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            pr->mapped[k] = nullptr;
+            return fail(FFNRM_ERR_CUDA, "cannot map rank %d's region: %s", k, cudaGetErrorString(e));
+        }
+    }
+    pr->connected = true;
+    return FFNRM_OK;
+}
+
+int ffnrm_peer_allreduce(ffnrm_peer *pr, const float *partial, int64_t elems, uint16_t *y16, float *y32,
+                         void *stream) {
+    if (!pr || !partial || (!y16 && !y32)) return fail(FFNRM_ERR_ARG, "null argument");
+    if (!pr->connected) return fail(FFNRM_ERR_STATE, "peer reduction not connected");
+    if (elems <= 0 || elems % 4 || elems > pr->max_elems)
+        return fail(FFNRM_ERR_ARG, "elems=%lld: a positive multiple of 4 up to %lld", (long long)elems,
+                    (long long)pr->max_elems);
+    if (!aligned(partial, 16) || (y32 && !aligned(y32, 16)) || (y16 && !aligned(y16, 8)))
+        return fail(FFNRM_ERR_ARG, "partial and y32 must be 16-byte aligned, y16 8-byte aligned");
+    DeviceGuard guard(pr->device);
+    ffnrm::PeerParams p{};
+    for (int k = 0; k < pr->world; ++k) {
+        p.recv[k] = static_cast<float *>(pr->mapped[k]);
+        p.flags[k] = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(pr->mapped[k]) + pr->recv_bytes);
+    }
+    p.partial = partial;
+    p.y16 = reinterpret_cast<__half *>(y16);
+    p.y32 = y32;
+    p.epoch = pr->counters;
+    p.done = pr->counters + 1;
+    p.status = pr->status;
+    p.elems = elems;
+    p.max_elems = pr->max_elems;
+    p.world = pr->world;
+    p.rank = pr->rank;
+    const int64_t per = (elems + ffnrm::kPeerMaxChunks - 1) / ffnrm::kPeerMaxChunks;
+    p.chunk = int(std::max<int64_t>(2048, (per + 3) / 4 * 4));
+    const int chunks = int((elems + p.chunk - 1) / p.chunk);
+    ffnrm::peer_allreduce_kernel<<<chunks, ffnrm::kPeerThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+    FFNRM_CUDA(cudaGetLastError());
+    return FFNRM_OK;
+}
+
+int ffnrm_peer_check(ffnrm_peer *pr, void *stream) {
+    if (!pr) return fail(FFNRM_ERR_ARG, "null argument");
+    DeviceGuard guard(pr->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int code = 0;
+    FFNRM_CUDA(cudaMemcpyAsync(&code, pr->status, sizeof(int), cudaMemcpyDeviceToHost, st));
+    FFNRM_CUDA(cudaStreamSynchronize(st));
+    if (code) {
+        FFNRM_CUDA(cudaMemsetAsync(pr->status, 0, sizeof(int), st));
+        FFNRM_CUDA(cudaStreamSynchronize(st));
+        return fail(FFNRM_ERR_TIMEOUT, "the peer reduction gave up waiting for another rank");
+    }
+    return FFNRM_OK;
+}
+
+int ffnrm_peer_destroy(ffnrm_peer *pr) {
+    if (!pr) return FFNRM_OK;
+    DeviceGuard guard(pr->device);
+    cudaDeviceSynchronize();
+    for (int k = 0; k < pr->world; ++k)
+        if (k != pr->rank && pr->mapped[k]) cudaIpcCloseMemHandle(pr->mapped[k]);
+    cudaFree(pr->region);
+    cudaFree(pr->counters);
+    cudaFree(pr->status);
+    cudaGetLastError();
+    delete pr;
     return FFNRM_OK;
 }
 

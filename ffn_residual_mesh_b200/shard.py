@@ -1,17 +1,24 @@
 """d_ff sharding across GPUs: one process per GPU, row-parallel down projection,
-one allreduce of the fp32 partial output per layer.
+one reduction of the fp32 partial output per layer.
 
 The reference has no multi-GPU code; this is the tensor-parallel split the path
 admits: gate/up output rows (d_ff) are independent, so rank k holds the contiguous
 rows ``shard_rows(F, N, k)`` of gate/up codes, alpha, its slice of the base sums,
 and the matching columns of the down weight. Its down projection yields a partial
-``y_k [T, D]``; ``sum_k y_k`` (NCCL allreduce over NVLink) is the layer output.
+``y_k [T, D]``; ``sum_k y_k`` is the layer output. The sum runs as one kernel per
+layer over NVLink (``ffnrm_peer_allreduce``: push partials into peer memory, per-chunk
+flags, sum in rank order, fp16 out); ``FFNRM_PEER_REDUCE=0`` selects an NCCL allreduce
+plus a cast instead.
 """
 from __future__ import annotations
 
+import ctypes
+import os
+
 import numpy as np
 
-from .engine import ResidualMesh, cast_f16
+from . import _native as N
+from .engine import ResidualMesh, _addr, _stream, cast_f16
 
 
 def shard_rows(d_ff: int, world: int, rank: int, align: int = 8) -> slice:
@@ -26,6 +33,36 @@ def shard_rows(d_ff: int, world: int, rank: int, align: int = 8) -> slice:
     return slice(begin, end)
 
 
+class PeerReduce:
+    """This rank's end of the NVLink layer-output reduction. Construction is collective:
+    every rank of ``group`` creates its receive region and the ranks exchange CUDA IPC
+    handles through the process group."""
+
+    def __init__(self, world, rank, device, max_elems, group=None):
+        import torch.distributed as dist
+        self._h = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * N.IPC_HANDLE_BYTES)()
+        N.check(N.lib().ffnrm_peer_create(ctypes.byref(self._h), device, world, rank, max_elems, handle))
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        table = (ctypes.c_uint8 * (N.IPC_HANDLE_BYTES * world)).from_buffer_copy(b"".join(handles))
+        N.check(N.lib().ffnrm_peer_connect(self._h, table))
+
+    def allreduce(self, partial, y16=None, y32=None, stream=None) -> None:
+        """y = sum over ranks of ``partial`` (f32), written as fp16 ``y16`` and/or f32 ``y32``."""
+        n = int(np.prod(partial.shape))
+        N.check(N.lib().ffnrm_peer_allreduce(self._h, _addr(partial), n, _addr(y16) if y16 is not None else None,
+                                             _addr(y32) if y32 is not None else None, _stream(stream)))
+
+    def check(self, stream=None) -> None:
+        N.check(N.lib().ffnrm_peer_check(self._h, _stream(stream)))
+
+    def close(self) -> None:
+        if self._h:
+            N.lib().ffnrm_peer_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+
 class ShardedFfnStack:
     """A ``ResidualMesh`` over this rank's d_ff shard plus the per-layer allreduce."""
 
@@ -37,6 +74,9 @@ class ShardedFfnStack:
         self.mesh = ResidualMesh(d_model, self.rows.stop - self.rows.start, residual_bits, n_layers, max_tokens,
                                  base_tile_rows, device)
         self._y32 = None
+        self.peer = None
+        if world > 1 and os.environ.get("FFNRM_PEER_REDUCE", "0") != "0":
+            self.peer = PeerReduce(world, rank, device, max_tokens * d_model, group=group)
 
     @property
     def d_ff(self) -> int:
@@ -56,6 +96,9 @@ class ShardedFfnStack:
         import torch.distributed as dist
         y32 = self._partial(z.shape[0], z.device)
         self.mesh.forward(layer, z, s, gate_base, up_base, fallback_tiles=fallback_tiles, y32=y32, stream=stream)
+        if self.peer is not None:
+            self.peer.allreduce(y32, y16=y16, stream=stream)
+            return
         dist.all_reduce(y32, group=self.group)
         cast_f16(y32, y16, stream=stream)
 
@@ -86,6 +129,15 @@ class ShardedFfnStack:
                 "y16": torch.empty(T, D, dtype=torch.float16, device=device)}
 
     def close(self):
+        if self.peer is not None:
+            # every rank has finished its reductions before any region is unmapped
+            import torch
+            import torch.distributed as dist
+            torch.cuda.synchronize()
+            self.peer.check()
+            dist.barrier(group=self.group)
+            self.peer.close()
+            self.peer = None
         self.mesh.close()
 
 

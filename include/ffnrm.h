@@ -138,6 +138,29 @@ int ffnrm_host_unregister(void *ptr);
 /* Convert f32 [n] -> fp16 [n] on `stream` (used after a cross-GPU allreduce of y_f32). */
 int ffnrm_cast_f16(const float *src, uint16_t *dst, int64_t n, void *stream);
 
+/* ---- Layer-output reduction of the d_ff-sharded stack over NVLink -------------------
+ * No counterpart in the reference, which runs on one device; it replaces the NCCL
+ * allreduce of the fp32 partial y_k plus ffnrm_cast_f16 in the sharded stack. One process
+ * per GPU on one node, 2..8 ranks. Each rank creates its peer object (a receive region
+ * shared through CUDA IPC), exchanges the FFNRM_IPC_HANDLE_BYTES handle with the other
+ * ranks (any host channel), and connects with all handles in rank order. Per layer,
+ * every rank calls ffnrm_peer_allreduce in the same order on its stream: one kernel
+ * pushes this rank's partial [elems] f32 to every rank, raises per-chunk flags, waits
+ * (bounded, about a second) for every rank's chunk, and writes y = sum in rank order as
+ * fp16 y16 and/or f32 y32 (identical on every rank). The call counter lives on the
+ * device, so the calls may be captured in a CUDA graph and replayed. elems: a positive
+ * multiple of 4 up to max_elems; partial and y32 16-byte aligned, y16 8-byte aligned.
+ * ffnrm_peer_check synchronises `stream` and reports FFNRM_ERR_TIMEOUT if a wait gave up
+ * (a rank stopped calling). Destroy only after every rank has finished its calls. */
+#define FFNRM_IPC_HANDLE_BYTES 64
+typedef struct ffnrm_peer ffnrm_peer;
+int ffnrm_peer_create(ffnrm_peer **out, int device, int world, int rank, int64_t max_elems, void *ipc_handle);
+int ffnrm_peer_connect(ffnrm_peer *peer, const void *ipc_handles);
+int ffnrm_peer_allreduce(ffnrm_peer *peer, const float *partial, int64_t elems, uint16_t *y16, float *y32,
+                         void *stream);
+int ffnrm_peer_check(ffnrm_peer *peer, void *stream);
+int ffnrm_peer_destroy(ffnrm_peer *peer);
+
 /* Device bytes held by loaded weights / workspace (for the bench's byte accounting). */
 int ffnrm_layer_bytes(ffnrm_ctx *ctx, int layer, int64_t *residual_bytes, int64_t *down_bytes);
 
