@@ -75,7 +75,7 @@ class ShardedFfnStack:
                                  base_tile_rows, device)
         self._y32 = None
         self.peer = None
-        if world > 1 and os.environ.get("FFNRM_PEER_REDUCE", "0") != "0":
+        if world > 1 and os.environ.get("FFNRM_PEER_REDUCE", "1") != "0":
             self.peer = PeerReduce(world, rank, device, max_tokens * d_model, group=group)
 
     @property
