@@ -895,9 +895,20 @@ int ffnrm_ffn_forward_host(ffnrm_ctx *ctx, int layer, const int8_t *z, const flo
     if ((rc = enqueue_residual(ctx, layer, ctx->z_dev[sl], ctx->s_dev[sl], tokens, nullptr, nullptr, nullptr, tiles_dev,
                                ctx->base_dev[sl][0], ctx->base_dev[sl][1], st)))
         return rc;
-    if ((rc = enqueue_down(ctx, layer, tokens, nullptr, ctx->y16_dev, st))) return rc;
+    // A page-locked, device-mapped y (cudaHostAlloc, or cudaHostRegister with mapping) is
+    // written by the down projection itself over PCIe; otherwise y goes through device
+    // staging and one copy back.
+    uint16_t *y_mapped = nullptr;
+    {
+        cudaPointerAttributes a{};
+        if (cudaPointerGetAttributes(&a, y_f16) == cudaSuccess && a.type == cudaMemoryTypeHost && a.devicePointer &&
+            aligned(a.devicePointer, 8))
+            y_mapped = static_cast<uint16_t *>(a.devicePointer);
+        cudaGetLastError();
+    }
+    if ((rc = enqueue_down(ctx, layer, tokens, nullptr, y_mapped ? y_mapped : ctx->y16_dev, st))) return rc;
     FFNRM_CUDA(cudaEventRecord(ctx->slot_free[sl], st));
-    FFNRM_CUDA(cudaMemcpyAsync(y_f16, ctx->y16_dev, size_t(tokens) * D * 2, cudaMemcpyDeviceToHost, st));
+    if (!y_mapped) FFNRM_CUDA(cudaMemcpyAsync(y_f16, ctx->y16_dev, size_t(tokens) * D * 2, cudaMemcpyDeviceToHost, st));
     return FFNRM_OK;
 }
 

@@ -124,7 +124,9 @@ int ffnrm_ffn_forward(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s
  * contraction runs on `stream`; the merge waits for the upload by event. This is
  * the double-buffered copy/compute pipeline of
  * src/exact_cpu_base_gpu_full_ffn_runner.cu:315-345, with one transfer per
- * projection instead of one per tile because the base arrives complete. y is
+ * projection instead of one per tile because the base arrives complete. A y_f16 in
+ * page-locked, device-mapped memory (cudaHostAlloc, or cudaHostRegister with mapping;
+ * 8-byte aligned) is written by the down projection directly over PCIe; any other y is
  * copied back on `stream`. Host buffers must stay valid until `stream` completes. */
 int ffnrm_ffn_forward_host(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s, int tokens,
                            const float *gate_base, const float *up_base, const uint8_t *fallback_tiles,
