@@ -1028,8 +1028,10 @@ int ffnrm_peer_allreduce(ffnrm_peer *pr, const float *partial, int64_t elems, ui
     const int64_t per = (elems + ffnrm::kPeerMaxChunks - 1) / ffnrm::kPeerMaxChunks;
     p.chunk = int(std::max<int64_t>(2048, (per + 3) / 4 * 4));
     const int chunks = int((elems + p.chunk - 1) / p.chunk);
-    ffnrm::peer_allreduce_kernel<<<chunks, ffnrm::kPeerThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
-    FFNRM_CUDA(cudaGetLastError());
+    // a dependent launch: its start overlaps the tail of the preceding kernel (the down
+    // projection, which releases its dependents early)
+    FFNRM_CUDA(launch_dependent(ffnrm::peer_allreduce_kernel, dim3(unsigned(chunks)), dim3(ffnrm::kPeerThreads), 0,
+                                static_cast<cudaStream_t>(stream), true, 1, p));
     return FFNRM_OK;
 }
 

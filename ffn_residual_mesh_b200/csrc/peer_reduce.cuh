@@ -48,6 +48,9 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_kernel(const Peer
     __shared__ int s_ok;
     const int c = blockIdx.x;
     const int64_t v0 = int64_t(c) * p.chunk / 4, v1 = min(p.elems, int64_t(c + 1) * p.chunk) / 4;  // float4 range
+    // Launched as a dependent of the down projection: the partial (and this rank's call
+    // counter, last written two kernels earlier) are read only after it has completed.
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
     if (threadIdx.x == 0) {
         s_ep = *reinterpret_cast<volatile uint32_t *>(p.epoch) + 1u;
         s_ok = 1;
