@@ -64,7 +64,7 @@ struct LayerDev {
     // for up)
     DevBuf pair, plane, pair_hi, alpha, beta, down;
     // low codes, one byte each, rows [128*rt, 128*rt+64) gate rows of tile rt then its up
-    // rows: the tensor-core A operand (built when batches of more than kGemvMaxTokens fit)
+    // rows: the tensor-core A operand (built when batches larger than the GEMV's fit)
     DevBuf codes8;
     CUtensorMap codes8_map;  // box 128 codes x 128 rows, 128-byte swizzle
     CUtensorMap down_map;    // TMA view of down [D][F16] fp16, box 64 x 128, 128-byte swizzle
@@ -173,6 +173,7 @@ struct ffnrm_ctx {
     bool slot_in_capture[2] = {false, false};
     int64_t launches = 0;
     int num_sms = 148;
+    int gemv_tokens = 2;  // FFNRM_GEMV_TOKENS: largest batch for the dp4a GEMV (measured crossover)
     // live profiling: event pairs around launches, resolved by ffnrm_profile_read
     bool prof = false;
     std::vector<cudaEvent_t> prof_pool;
@@ -498,13 +499,17 @@ int launch_residual_tc_t(ffnrm_ctx *ctx, const LayerDev &L, ffnrm::ResidualParam
     return FFNRM_OK;
 }
 
-// T <= 4: dp4a GEMV on the 2-bit records (HBM-bound); larger batches: tcgen05 kind::i8
+// T <= 2: dp4a GEMV on the 2-bit records (3..4 too without the tensor-core path; measured
+// crossover: T = 3 and 4 run faster on the tensor cores); larger batches: tcgen05 kind::i8
 // tiles on the byte codes, or mma.sync tiles when fallback tiles need the unsplit codes.
 template <int RB>
 int launch_residual_rb(ffnrm_ctx *ctx, const LayerDev &L, ffnrm::ResidualParams &p, bool half, cudaStream_t st) {
-    if (p.T == 1) return launch_residual_tt<RB, 1>(ctx, p, half, st);
-    if (p.T == 2) return launch_residual_tt<RB, 2>(ctx, p, half, st);
-    if (p.T <= 4) return launch_residual_tt<RB, 4>(ctx, p, half, st);
+    const bool tc_ok = p.fallback_tiles == nullptr && L.codes8.ptr && ctx->use_umma;
+    if (p.T <= std::min(ctx->gemv_tokens, ffnrm::kGemvMaxTokens) || (p.T <= ffnrm::kGemvMaxTokens && !tc_ok)) {
+        if (p.T == 1) return launch_residual_tt<RB, 1>(ctx, p, half, st);
+        if (p.T == 2) return launch_residual_tt<RB, 2>(ctx, p, half, st);
+        return launch_residual_tt<RB, 4>(ctx, p, half, st);
+    }
     if (p.fallback_tiles == nullptr && L.codes8.ptr && ctx->use_umma &&
         ffnrm::ResTcCfg<32, false>::smem(p.G, 2) <= 227 * 1024) {
         if (p.T <= 16) return half ? launch_residual_tc_t<16, true>(ctx, L, p, st) : launch_residual_tc_t<16, false>(ctx, L, p, st);
@@ -682,6 +687,7 @@ int ffnrm_create(ffnrm_ctx **out, int device, const ffnrm_config *cfg) {
     ctx->G = c.d_model / 32;
     ctx->layers.resize(size_t(c.n_layers));
     if (const char *e = std::getenv("FFNRM_RESIDUAL_MMA_SYNC")) ctx->use_umma = std::strcmp(e, "1") != 0;
+    if (const char *e = std::getenv("FFNRM_GEMV_TOKENS")) ctx->gemv_tokens = std::max(1, std::atoi(e));
     cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
     const size_t TF = size_t(c.max_tokens) * c.d_ff, TD = size_t(c.max_tokens) * c.d_model;
     const size_t F16 = (size_t(c.d_ff) + 15) / 16 * 16;
@@ -787,7 +793,7 @@ int ffnrm_load_layer(ffnrm_ctx *ctx, int layer, const ffnrm_layer_weights *w) {
         if (rc == FFNRM_OK) rc = upload_scales(L.beta, beta, F, G, L.scales_half);
     }
     if (rc == FFNRM_OK) rc = upload_scales(L.alpha, alpha, F, G, L.scales_half);
-    if (rc == FFNRM_OK && ctx->cfg.max_tokens > ffnrm::kGemvMaxTokens) {
+    if (rc == FFNRM_OK && ctx->cfg.max_tokens > std::min(ctx->gemv_tokens, ffnrm::kGemvMaxTokens)) {
         const uint8_t *src[2] = {lo[0].data(), lo[1].data()};
         pack_codes8(src, F, D, packed);
         rc = upload(L.codes8, packed.data(), packed.size());

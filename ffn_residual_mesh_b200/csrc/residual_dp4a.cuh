@@ -69,7 +69,7 @@ __device__ __forceinline__ void store_h(const ResidualParams &p, int tok, int ro
 }
 
 constexpr int kResWarps = 4;  // per projection; the CTA runs 2 * kResWarps warps
-constexpr int kGemvMaxTokens = 4;  // larger batches go to the tensor cores
+constexpr int kGemvMaxTokens = 4;  // largest GEMV instance (batches of 3-4 prefer the tensor cores)
 
 // Each warp streams its chunk records through a cp.async ring of kGemvBufs windows of
 // kGemvWin chunks, so about kGemvBufs * kGemvWin chunks per lane are in flight while it

@@ -2,7 +2,7 @@
 // exact int32 group dots with tcgen05.mma kind::i8 (u8 codes x s8 activations).
 //
 // Replaces residual_kernel (src/exact_residual_cuda_runner.cu:122-159) for batches of
-// more than kGemvMaxTokens tokens without fallback tiles.
+// 3 or more tokens (the GEMV keeps 1-2) without fallback tiles.
 //
 // The A operand is the layer's low codes as one byte per code, stored at load time
 // row-tiled: rows [128*rt, 128*rt+64) are gate rows 64*rt.. and the next 64 the up rows
