@@ -25,8 +25,10 @@
 #include "ffnrm_common.cuh"
 #include "residual_dp4a.cuh"
 #include "residual_mma.cuh"
+#include "pack.cuh"
 #include "peer_reduce.cuh"
 #include "residual_tc.cuh"
+#include "residual_umma.cuh"
 
 namespace {
 
@@ -154,10 +156,13 @@ struct ffnrm_ctx {
     ffnrm_config cfg{};
     int G = 0;
     std::vector<LayerDev> layers;
+    DevBuf scratch;  // load-time decode scratch (grown on demand, kept for later layers)
     // workspace
-    float *res[2] = {nullptr, nullptr};  // [Tm, F]
     int *err = nullptr;                  // device error word written by bounded waits
-    bool use_umma = true;                // tcgen05 residual for T >= 5 (FFNRM_RESIDUAL_MMA_SYNC=1 disables)
+    // T >= 3 residual: 1 = tcgen05 on byte codes where possible, packed records otherwise
+    // (default); 0 = packed records only (no byte codes are built); 2 = mma.sync tiles
+    // (FFNRM_RESIDUAL_KERNEL=bytes|packed|mma)
+    int res_kernel = 1;
     CUtensorMap h_map[4][2];             // h hi/lo views for token tiles 16, 32, 64, 128
     __half *h_hi = nullptr, *h_lo = nullptr;  // [Tm, F16] h = SiLU(g)*u as fp16 hi + lo
     // host-streamed mode staging, double-buffered per call
@@ -211,148 +216,37 @@ void dev_free(DevBuf &b) {
     b.bytes = 0;
 }
 
-int upload(DevBuf &b, const void *host, size_t bytes) {
-    int rc = dev_alloc(b, bytes);
-    if (rc) return rc;
-    FFNRM_CUDA(cudaMemcpy(b.ptr, host, bytes, cudaMemcpyHostToDevice));
-    return FFNRM_OK;
-}
+// Grid of a grid-stride load-time kernel over n outputs.
+unsigned pack_blocks(int64_t n) { return unsigned(std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 148 * 16))); }
 
-// Pack bits [shift, shift+1] of codes [F, D] into the interleaved pair layout
-// [F32][G/2][32][16 B] (see ffnrm_common.cuh). Padding rows are zero.
-// Record of projection `proj`, row r, chunk c in the row-tiled layout.
-int64_t tiled_record(int proj, int64_t r, int64_t C, int64_t c) {
-    return ((r / 64) * C + c) * 128 + proj * 64 + (r % 64);
-}
+// Device view of one input array of ffnrm_load_layer: the caller's pointer when it is
+// device memory of the context's device, else a device copy of the host data (owned).
+struct Staged {
+    const void *dev = nullptr;
+    void *owned = nullptr;
+    ~Staged() {
+        if (owned) cudaFree(owned);
+    }
+};
 
-// Pack bits shift..shift+1 of both projections' codes [F, D] into pair records
-// [F64][G/2][2][64][16 B].
-void pack_pair_tiles(const uint8_t *const q[2], int shift, int64_t F, int64_t D, std::vector<uint8_t> &out) {
-    const int64_t F64 = (F + 63) / 64, C = D / 64;
-    out.assign(size_t(F64 * C * 128 * 16), 0);
-    for (int proj = 0; proj < 2; ++proj)
-        for (int64_t r = 0; r < F; ++r) {
-            const uint8_t *src = q[proj] + r * D;
-            for (int64_t c = 0; c < C; ++c) {
-                uint32_t *rec = reinterpret_cast<uint32_t *>(out.data() + tiled_record(proj, r, C, c) * 16);
-                for (int j = 0; j < 4; ++j) {
-                    const uint8_t *codes = src + 64 * c + 16 * j;  // group 2c + (j>>1), half j&1
-                    uint32_t w = 0;
-                    for (int i = 0; i < 4; ++i)
-                        for (int b = 0; b < 4; ++b) w |= uint32_t((codes[4 * i + b] >> shift) & 3) << (8 * b + 2 * i);
-                    rec[j] = w;
-                }
-            }
-        }
-}
-
-// Pack bit `bit` of both projections' codes [F, D] into plane records [F64][G/2][2][64][8 B].
-void pack_plane_tiles(const uint8_t *const q[2], int bit, int64_t F, int64_t D, std::vector<uint8_t> &out) {
-    const int64_t F64 = (F + 63) / 64, C = D / 64;
-    out.assign(size_t(F64 * C * 128 * 8), 0);
-    for (int proj = 0; proj < 2; ++proj)
-        for (int64_t r = 0; r < F; ++r) {
-            const uint8_t *src = q[proj] + r * D;
-            for (int64_t c = 0; c < C; ++c) {
-                uint32_t *rec = reinterpret_cast<uint32_t *>(out.data() + tiled_record(proj, r, C, c) * 8);
-                for (int j = 0; j < 2; ++j) {
-                    const uint8_t *codes = src + 64 * c + 32 * j;
-                    uint32_t w = 0;
-                    for (int i = 0; i < 8; ++i)
-                        for (int b = 0; b < 4; ++b) w |= uint32_t((codes[4 * i + b] >> bit) & 1) << (8 * b + i);
-                    rec[j] = w;
-                }
-            }
-        }
-}
-
-// Decode one projection's input codes into full / low code bytes [F, D].
-// Returns in `lo` the r-bit low codes and, when high codes are available, in `full` the
-// complete Q4 codes (`have_full` = true).
-int decode_codes(const ffnrm_layer_weights *w, const uint8_t *codes, const uint8_t *high, int r, int64_t F,
-                 int64_t D, std::vector<uint8_t> &lo, std::vector<uint8_t> &full, bool &have_full) {
-    const int64_t n = F * D;
-    lo.resize(size_t(n));
-    have_full = false;
-    const uint8_t mask = uint8_t((1 << r) - 1);
-    if (w->codes_format == FFNRM_CODES_Q4_BYTES) {
-        for (int64_t i = 0; i < n; ++i) {
-            if (codes[i] > 15) return fail(FFNRM_ERR_ARG, "Q4 codes must be in [0, 15]");
-            lo[size_t(i)] = codes[i] & mask;
-        }
-        if (w->keep_fallback) {
-            full.assign(codes, codes + n);
-            have_full = true;
-        }
+int stage_in(int device, const void *src, size_t bytes, Staged &out) {
+    if (!src || !bytes) return FFNRM_OK;
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, src) == cudaSuccess &&
+        (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged)) {
+        if (a.type == cudaMemoryTypeDevice && a.device != device)
+            return fail(FFNRM_ERR_ARG, "a weight array lives on device %d, the context on device %d", a.device, device);
+        out.dev = src;
         return FFNRM_OK;
     }
-    if (w->codes_format == FFNRM_CODES_QLO2_ROWPACKED) {
-        if (r != 2) return fail(FFNRM_ERR_ARG, "QLO2 row-packed codes require residual_bits == 2");
-        for (int64_t i = 0; i < n; ++i) lo[size_t(i)] = (codes[i / 4] >> (2 * (i & 3))) & 3;
-    } else if (w->codes_format == FFNRM_CODES_BITPLANES) {
-        const int64_t plane = n / 8;
-        for (int64_t i = 0; i < n; ++i) {
-            uint8_t v = 0;
-            for (int b = 0; b < r; ++b) v |= uint8_t(((codes[b * plane + i / 8] >> (i & 7)) & 1) << b);
-            lo[size_t(i)] = v;
-        }
-    } else {
-        return fail(FFNRM_ERR_ARG, "unknown codes_format %d", w->codes_format);
+    cudaGetLastError();
+    if (cudaMalloc(&out.owned, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(FFNRM_ERR_NOMEM, "cudaMalloc of %zu staging bytes failed", bytes);
     }
-    if (high) {
-        const int64_t plane = n / 8;
-        const int hb = 4 - r;
-        full.resize(size_t(n));
-        for (int64_t i = 0; i < n; ++i) {
-            uint8_t v = 0;
-            for (int b = 0; b < hb; ++b) v |= uint8_t(((high[b * plane + i / 8] >> (i & 7)) & 1) << b);
-            full[size_t(i)] = uint8_t((v << r) | lo[size_t(i)]);
-        }
-        have_full = true;
-    }
+    FFNRM_CUDA(cudaMemcpy(out.owned, src, bytes, cudaMemcpyHostToDevice));
+    out.dev = out.owned;
     return FFNRM_OK;
-}
-
-bool all_half_exact(const float *v, int64_t n) {
-    for (int64_t i = 0; i < n; ++i) {
-        const float back = __half2float(__float2half_rn(v[i]));
-        if (!(back == v[i]) && !(std::isnan(v[i]) && std::isnan(back))) return false;
-    }
-    return true;
-}
-
-// Per-group scales [F, G] -> interleaved [F32][G/2][32][2] (fp16 or f32).
-// Both projections' scales [F, G] -> [F64][G/2][2][64][2], fp16 when lossless.
-int upload_scales(DevBuf &b, const float *const v[2], int64_t F, int64_t G, bool as_half) {
-    const int64_t F64 = (F + 63) / 64, C = G / 2, n = F64 * C * 128 * 2;
-    std::vector<float> il(size_t(n), 0.f);
-    for (int proj = 0; proj < 2; ++proj)
-        for (int64_t r = 0; r < F; ++r)
-            for (int64_t c = 0; c < C; ++c)
-                for (int e = 0; e < 2; ++e) il[size_t(tiled_record(proj, r, C, c) * 2 + e)] = v[proj][r * G + 2 * c + e];
-    if (!as_half) return upload(b, il.data(), size_t(n) * 4);
-    std::vector<__half> h{};
-    h.resize(size_t(n));
-    for (int64_t i = 0; i < n; ++i) h[size_t(i)] = __float2half_rn(il[size_t(i)]);
-    return upload(b, h.data(), size_t(n) * 2);
-}
-
-// fp16 down [D, ld] (F used columns) -> row-major [D][F16] with zero columns F..F16-1.
-int upload_down(DevBuf &b, const uint16_t *down, int64_t ld, int64_t F, int64_t D) {
-    const int64_t F16 = (F + 15) / 16 * 16;
-    std::vector<uint16_t> rm(size_t(D * F16), 0);
-    for (int64_t o = 0; o < D; ++o) std::memcpy(rm.data() + o * F16, down + o * ld, size_t(F) * 2);
-    return upload(b, rm.data(), rm.size() * 2);
-}
-
-// Low codes of both projections [F, D] -> [F64 * 128][D] bytes, tile rows stacked gate
-// then up.
-void pack_codes8(const uint8_t *const q[2], int64_t F, int64_t D, std::vector<uint8_t> &out) {
-    const int64_t F64 = (F + 63) / 64;
-    out.assign(size_t(F64 * 128 * D), 0);
-    for (int proj = 0; proj < 2; ++proj)
-        for (int64_t r = 0; r < F; ++r)
-            std::memcpy(out.data() + ((r / 64) * 128 + proj * 64 + r % 64) * D, q[proj] + r * D, size_t(D));
 }
 
 // 2-D u8 tensor [rows][cols] in boxes of 128 x box_rows with 128-byte swizzle.
@@ -499,25 +393,113 @@ int launch_residual_tc_t(ffnrm_ctx *ctx, const LayerDev &L, ffnrm::ResidualParam
     return FFNRM_OK;
 }
 
-// T <= 2: dp4a GEMV on the 2-bit records (3..4 too without the tensor-core path; measured
-// crossover: T = 3 and 4 run faster on the tensor cores); larger batches: tcgen05 kind::i8
-// tiles on the byte codes, or mma.sync tiles when fallback tiles need the unsplit codes.
+// Shared-memory layout of the packed-record tcgen05 residual for token tile N within
+// `budget` bytes. Ring depths (S1 + S3 + SB <= 32 producer lanes) are chosen by a score
+// of what each ring has to cover: code records (S1) one HBM round trip (~8 K tiles at the
+// decode streaming rate), scales (S3) that plus the converter/MMA/drain lag (~16), the
+// activation tiles (SB) an L2 round trip (~4), widened codes (S2) 2-3. The epilogue's
+// up-row exchange [64][N+1] f32 reuses the code and activation rings.
+ffnrm::UmLayout umma_layout(int N, bool has_pair, bool has_plane, bool has_hi, bool alpha_half, bool fb,
+                            size_t budget) {
+    const int a = 128 * ffnrm::kUmKTile, b = N * ffnrm::kUmKTile;
+    ffnrm::UmLayout L{}, best{};
+    int off = 0;
+    L.off_pair = has_pair ? off : -1;
+    off += has_pair ? 4096 : 0;
+    L.off_plane = has_plane ? off : -1;
+    off += has_plane ? 2048 : 0;
+    L.off_hi = has_hi ? off : -1;
+    off += has_hi ? 4096 : 0;
+    L.src_bytes = std::max(off, 16);
+    L.sc_bytes = (alpha_half ? 1024 : 2048) * (fb ? 2 : 1);
+    const int win = 2 * ffnrm::kUmWin * (N + 4) * 4 * (fb ? 2 : 1);
+    const int bars = (2 * (ffnrm::kUmMaxS1 + ffnrm::kUmMaxS2 + ffnrm::kUmMaxS3 + ffnrm::kUmMaxSB) + 2 * 4 + 1) * 8 + 16;
+    const int xch = 64 * (N + 1) * 4;
+    best.total = -1;
+    int best_score = -1;
+    for (int S2 = 2; S2 <= 3; ++S2)
+        for (int SB = 2; SB <= ffnrm::kUmMaxSB; ++SB)
+            for (int S1 = 3; S1 <= ffnrm::kUmMaxS1; ++S1)
+                for (int S3 = 4; S3 <= std::min(ffnrm::kUmMaxS3, 32 - S1 - SB); ++S3) {
+                    L.S1 = S1;
+                    L.S2 = S2;
+                    L.S3 = S3;
+                    L.SB = SB;
+                    L.b_off = S2 * a;
+                    L.src_off = L.b_off + SB * b;
+                    L.sc_off = L.src_off + S1 * L.src_bytes;
+                    L.win_off = L.sc_off + S3 * L.sc_bytes;
+                    L.bar_off = (L.win_off + win + 7) / 8 * 8;
+                    L.total = L.bar_off + bars;
+                    if (size_t(L.total) + 1024 > budget || L.src_off < xch) continue;
+                    const int score = 4 * std::min(S1, 8) + 2 * std::min(S3, 16) + 4 * std::min(SB, 4) + 3 * S2 +
+                                      std::min(S3, 24) / 4 + std::min(SB, 8) / 4;
+                    if (score > best_score || (score == best_score && L.total < best.total)) {
+                        best_score = score;
+                        best = L;
+                    }
+                }
+    return best;
+}
+
+template <int N>
+int launch_residual_umma_t(ffnrm_ctx *ctx, const LayerDev &L, ffnrm::ResidualParams &p, cudaStream_t st) {
+    using Cfg = ffnrm::UmCfg<N>;
+    ffnrm::UmParams P{};
+    P.rbits = ctx->cfg.residual_bits;
+    P.has_pair = L.pair.ptr != nullptr;
+    P.alpha_half = L.scales_half ? 1 : 0;
+    P.fb = p.fallback_tiles != nullptr;
+    const size_t budget = Cfg::minb == 2 ? 113 * 1024 : 227 * 1024;
+    P.L = umma_layout(N, P.has_pair, P.rbits != 2, P.fb && L.pair_hi.ptr, L.scales_half, P.fb, budget);
+    if (P.L.total < 0) return fail(FFNRM_ERR_ARG, "no shared-memory layout for the tensor-core residual (N=%d)", N);
+    const size_t smem = size_t(P.L.total) + 1024;
+    CUtensorMap zm;
+    if (!make_z_map(&zm, p.z, uint64_t(p.D), uint64_t(p.T), N))
+        return fail(FFNRM_ERR_CUDA, "cuTensorMapEncodeTiled rejected the activations");
+    void (*kern)(const CUtensorMap, const ffnrm::UmParams);
+    if constexpr (Cfg::minb == 2)
+        kern = p.dots ? ffnrm::residual_umma_kernel2<N, true> : ffnrm::residual_umma_kernel2<N, false>;
+    else
+        kern = p.dots ? ffnrm::residual_umma_kernel1<N, true> : ffnrm::residual_umma_kernel1<N, false>;
+    FFNRM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+    p.row_blocks = (p.F + 31) / 32;
+    p.err = ctx->err;
+    P.p = p;
+    dim3 grid(unsigned((p.T + N - 1) / N), unsigned((p.F + 63) / 64));
+    ProfScope prof(ctx, st, FFNRM_KERNEL_RESIDUAL);
+    FFNRM_CUDA(launch_dependent(kern, grid, dim3(Cfg::threads), smem, st, true, 1, zm, P));
+    ctx->launches++;
+    return FFNRM_OK;
+}
+
+// T <= 2 (FFNRM_GEMV_TOKENS): dp4a GEMV on the packed records. Larger batches: tcgen05
+// kind::i8 tiles - on the byte codes (token tiles of 16 or 32) when the layer has them and
+// no fallback tile is flagged; otherwise, fallback tiles included, on the packed records
+// widened to bytes in shared memory (token tiles of 16, 32, 64, 128). The mma.sync tiles
+// remain selectable for comparison (FFNRM_RESIDUAL_KERNEL=mma).
 template <int RB>
 int launch_residual_rb(ffnrm_ctx *ctx, const LayerDev &L, ffnrm::ResidualParams &p, bool half, cudaStream_t st) {
-    const bool tc_ok = p.fallback_tiles == nullptr && L.codes8.ptr && ctx->use_umma;
-    if (p.T <= std::min(ctx->gemv_tokens, ffnrm::kGemvMaxTokens) || (p.T <= ffnrm::kGemvMaxTokens && !tc_ok)) {
+    if (p.T <= std::min(ctx->gemv_tokens, ffnrm::kGemvMaxTokens)) {
         if (p.T == 1) return launch_residual_tt<RB, 1>(ctx, p, half, st);
         if (p.T == 2) return launch_residual_tt<RB, 2>(ctx, p, half, st);
         return launch_residual_tt<RB, 4>(ctx, p, half, st);
     }
-    if (p.fallback_tiles == nullptr && L.codes8.ptr && ctx->use_umma &&
+    if (ctx->res_kernel == 2) {
+        if (p.T <= ffnrm::kGemvMaxTokens) return launch_residual_tt<RB, 4>(ctx, p, half, st);
+        if (p.T <= 8) return launch_residual_mma_nt<RB, 1>(ctx, p, half, st);
+        if (p.T <= 16) return launch_residual_mma_nt<RB, 2>(ctx, p, half, st);
+        return launch_residual_mma_nt<RB, 4>(ctx, p, half, st);  // 32-token tiles (64 would spill)
+    }
+    if (ctx->res_kernel == 1 && p.fallback_tiles == nullptr && L.codes8.ptr &&
         ffnrm::ResTcCfg<32, false>::smem(p.G, 2) <= 227 * 1024) {
         if (p.T <= 16) return half ? launch_residual_tc_t<16, true>(ctx, L, p, st) : launch_residual_tc_t<16, false>(ctx, L, p, st);
         return half ? launch_residual_tc_t<32, true>(ctx, L, p, st) : launch_residual_tc_t<32, false>(ctx, L, p, st);
     }
-    if (p.T <= 8) return launch_residual_mma_nt<RB, 1>(ctx, p, half, st);
-    if (p.T <= 16) return launch_residual_mma_nt<RB, 2>(ctx, p, half, st);
-    return launch_residual_mma_nt<RB, 4>(ctx, p, half, st);  // 32-token tiles (64 would spill)
+    if (p.T <= 16) return launch_residual_umma_t<16>(ctx, L, p, st);
+    if (p.T <= 32) return launch_residual_umma_t<32>(ctx, L, p, st);
+    if (p.T <= 64) return launch_residual_umma_t<64>(ctx, L, p, st);
+    return launch_residual_umma_t<128>(ctx, L, p, st);
 }
 
 // Residual contraction of both projections. Residual mode (gate_base == nullptr): writes
@@ -686,14 +668,14 @@ int ffnrm_create(ffnrm_ctx **out, int device, const ffnrm_config *cfg) {
     ctx->cfg = c;
     ctx->G = c.d_model / 32;
     ctx->layers.resize(size_t(c.n_layers));
-    if (const char *e = std::getenv("FFNRM_RESIDUAL_MMA_SYNC")) ctx->use_umma = std::strcmp(e, "1") != 0;
+    if (const char *e = std::getenv("FFNRM_RESIDUAL_KERNEL"))
+        ctx->res_kernel = std::strcmp(e, "packed") == 0 ? 0 : std::strcmp(e, "mma") == 0 ? 2 : 1;
     if (const char *e = std::getenv("FFNRM_GEMV_TOKENS")) ctx->gemv_tokens = std::max(1, std::atoi(e));
     cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
     const size_t TF = size_t(c.max_tokens) * c.d_ff, TD = size_t(c.max_tokens) * c.d_model;
     const size_t F16 = (size_t(c.d_ff) + 15) / 16 * 16;
     const int ntiles = (c.d_ff + c.base_tile_rows - 1) / c.base_tile_rows;
-    bool ok = cudaMalloc(&ctx->res[0], TF * 4) == cudaSuccess && cudaMalloc(&ctx->res[1], TF * 4) == cudaSuccess &&
-              cudaMalloc(&ctx->err, sizeof(int)) == cudaSuccess && cudaMemset(ctx->err, 0, sizeof(int)) == cudaSuccess &&
+    bool ok = cudaMalloc(&ctx->err, sizeof(int)) == cudaSuccess && cudaMemset(ctx->err, 0, sizeof(int)) == cudaSuccess &&
               cudaMalloc(&ctx->h_hi, size_t(c.max_tokens) * F16 * 2) == cudaSuccess &&
               cudaMalloc(&ctx->h_lo, size_t(c.max_tokens) * F16 * 2) == cudaSuccess &&
               cudaMalloc(&ctx->y16_dev, TD * 2) == cudaSuccess;
@@ -728,8 +710,7 @@ int ffnrm_destroy(ffnrm_ctx *ctx) {
     DeviceGuard guard(ctx->device);
     cudaDeviceSynchronize();
     for (auto &L : ctx->layers) free_layer(L);
-    cudaFree(ctx->res[0]);
-    cudaFree(ctx->res[1]);
+    dev_free(ctx->scratch);
     cudaFree(ctx->err);
     cudaFree(ctx->h_hi);
     cudaFree(ctx->h_lo);
@@ -754,57 +735,106 @@ int ffnrm_load_layer(ffnrm_ctx *ctx, int layer, const ffnrm_layer_weights *w) {
     if (layer < 0 || layer >= ctx->cfg.n_layers) return fail(FFNRM_ERR_ARG, "layer %d out of range", layer);
     if (!w->gate_codes || !w->up_codes || !w->gate_alpha || !w->up_alpha || !w->down)
         return fail(FFNRM_ERR_ARG, "codes, alpha and down are required");
-    const int64_t F = ctx->cfg.d_ff, D = ctx->cfg.d_model, G = ctx->G;
+    const int64_t F = ctx->cfg.d_ff, D = ctx->cfg.d_model, G = ctx->G, n = F * D;
     const int r = ctx->cfg.residual_bits;
+    const int fmt = w->codes_format;
     if (w->down_ld < F) return fail(FFNRM_ERR_ARG, "down_ld=%lld must be >= d_ff=%lld", (long long)w->down_ld, (long long)F);
+    if (fmt != FFNRM_CODES_Q4_BYTES && fmt != FFNRM_CODES_QLO2_ROWPACKED && fmt != FFNRM_CODES_BITPLANES)
+        return fail(FFNRM_ERR_ARG, "unknown codes_format %d", fmt);
+    if (fmt == FFNRM_CODES_QLO2_ROWPACKED && r != 2)
+        return fail(FFNRM_ERR_ARG, "QLO2 row-packed codes require residual_bits == 2");
+    const bool want_hi = fmt == FFNRM_CODES_Q4_BYTES ? w->keep_fallback != 0 : (w->gate_high && w->up_high);
+    const bool have_beta = w->gate_beta && w->up_beta;
+    if (want_hi && !have_beta) return fail(FFNRM_ERR_ARG, "fallback high codes need gate_beta and up_beta");
     DeviceGuard guard(ctx->device);
     LayerDev &L = ctx->layers[size_t(layer)];
     free_layer(L);
-    const bool want_hi = w->codes_format == FFNRM_CODES_Q4_BYTES ? w->keep_fallback != 0 : (w->gate_high && w->up_high);
-    const bool have_beta = w->gate_beta && w->up_beta;
     L.has_fallback = want_hi && have_beta;
-    if (want_hi && !have_beta) return fail(FFNRM_ERR_ARG, "fallback high codes need gate_beta and up_beta");
-    L.scales_half = all_half_exact(w->gate_alpha, F * G) && all_half_exact(w->up_alpha, F * G) &&
-                    (!L.has_fallback || (all_half_exact(w->gate_beta, F * G) && all_half_exact(w->up_beta, F * G)));
-    const uint8_t *codes[2] = {w->gate_codes, w->up_codes};
-    const uint8_t *high[2] = {w->gate_high, w->up_high};
-    const float *alpha[2] = {w->gate_alpha, w->up_alpha};
-    const float *beta[2] = {w->gate_beta, w->up_beta};
-    std::vector<uint8_t> lo[2], full[2], packed;
-    bool have_full[2] = {false, false};
+    const size_t code_bytes = fmt == FFNRM_CODES_Q4_BYTES ? size_t(n) : fmt == FFNRM_CODES_QLO2_ROWPACKED ? size_t(n / 4)
+                                                                                                           : size_t(r * n / 8);
+    // Stage every input on the device, then decode and pack there.
+    Staged codes[2], high[2], alpha[2], beta[2];
+    const uint8_t *cin[2] = {w->gate_codes, w->up_codes}, *hin[2] = {w->gate_high, w->up_high};
+    const float *ain[2] = {w->gate_alpha, w->up_alpha}, *bin[2] = {w->gate_beta, w->up_beta};
     int rc = FFNRM_OK;
-    for (int q = 0; q < 2 && rc == FFNRM_OK; ++q)
-        rc = decode_codes(w, codes[q], L.has_fallback ? high[q] : nullptr, r, F, D, lo[q], full[q], have_full[q]);
-    if (rc == FFNRM_OK && (r != 1 || L.has_fallback)) {
+    for (int q = 0; q < 2 && rc == FFNRM_OK; ++q) {
+        rc = stage_in(ctx->device, cin[q], code_bytes, codes[q]);
+        if (rc == FFNRM_OK && L.has_fallback && fmt != FFNRM_CODES_Q4_BYTES)
+            rc = stage_in(ctx->device, hin[q], size_t((4 - r) * n / 8), high[q]);
+        if (rc == FFNRM_OK) rc = stage_in(ctx->device, ain[q], size_t(F * G) * 4, alpha[q]);
+        if (rc == FFNRM_OK && L.has_fallback) rc = stage_in(ctx->device, bin[q], size_t(F * G) * 4, beta[q]);
+    }
+    if (rc) return rc;
+    // scratch: low codes [2][n], full codes [2][n] (fallback, unless given as Q4 bytes), two flags
+    const bool full_scratch = L.has_fallback && fmt != FFNRM_CODES_Q4_BYTES;
+    const size_t need = size_t(n) * (full_scratch ? 4 : 2) + 16;
+    if (ctx->scratch.bytes < need) {
+        dev_free(ctx->scratch);
+        if ((rc = dev_alloc(ctx->scratch, need))) return rc;
+    }
+    uint8_t *lo[2] = {static_cast<uint8_t *>(ctx->scratch.ptr), static_cast<uint8_t *>(ctx->scratch.ptr) + n};
+    const uint8_t *full[2] = {nullptr, nullptr};
+    if (L.has_fallback)
+        for (int q = 0; q < 2; ++q)
+            full[q] = fmt == FFNRM_CODES_Q4_BYTES ? static_cast<const uint8_t *>(codes[q].dev)
+                                                  : static_cast<uint8_t *>(ctx->scratch.ptr) + (2 + q) * n;
+    int *flags = reinterpret_cast<int *>(static_cast<uint8_t *>(ctx->scratch.ptr) + size_t(n) * (full_scratch ? 4 : 2));
+    FFNRM_CUDA(cudaMemset(flags, 0, 2 * sizeof(int)));
+    for (int q = 0; q < 2; ++q)
+        ffnrm::decode_codes_kernel<<<pack_blocks(n), 256>>>(fmt, static_cast<const uint8_t *>(codes[q].dev),
+                                                           static_cast<const uint8_t *>(high[q].dev), r, n, lo[q],
+                                                           full_scratch ? const_cast<uint8_t *>(full[q]) : nullptr, flags);
+    for (int q = 0; q < 2; ++q) {
+        ffnrm::half_exact_kernel<<<pack_blocks(F * G), 256>>>(static_cast<const float *>(alpha[q].dev), F * G, flags + 1);
+        if (L.has_fallback)
+            ffnrm::half_exact_kernel<<<pack_blocks(F * G), 256>>>(static_cast<const float *>(beta[q].dev), F * G,
+                                                                  flags + 1);
+    }
+    FFNRM_CUDA(cudaGetLastError());
+    int hflags[2] = {0, 0};
+    FFNRM_CUDA(cudaMemcpy(hflags, flags, sizeof(hflags), cudaMemcpyDeviceToHost));
+    if (hflags[0]) return fail(FFNRM_ERR_ARG, "Q4 codes must be in [0, 15]");
+    L.scales_half = hflags[1] == 0;
+    const int64_t F64 = (F + 63) / 64, C = D / 64, recs = F64 * C * 128;
+    if ((r != 1 || L.has_fallback) && (rc = dev_alloc(L.pair, size_t(recs) * 16)) == FFNRM_OK) {
         // bits 0-1 of the full code equal the low two residual bits for r >= 2
-        const uint8_t *src[2] = {have_full[0] ? full[0].data() : lo[0].data(), have_full[1] ? full[1].data() : lo[1].data()};
-        pack_pair_tiles(src, 0, F, D, packed);
-        rc = upload(L.pair, packed.data(), packed.size());
+        const uint8_t *s0 = L.has_fallback ? full[0] : lo[0], *s1 = L.has_fallback ? full[1] : lo[1];
+        ffnrm::pack_pair_kernel<<<pack_blocks(recs), 256>>>(s0, s1, 0, F, D, static_cast<uint4 *>(L.pair.ptr));
     }
-    if (rc == FFNRM_OK && r != 2) {
-        const uint8_t *src[2] = {lo[0].data(), lo[1].data()};
-        pack_plane_tiles(src, r == 1 ? 0 : 2, F, D, packed);
-        rc = upload(L.plane, packed.data(), packed.size());
-    }
-    if (rc == FFNRM_OK && L.has_fallback) {
-        const uint8_t *src[2] = {full[0].data(), full[1].data()};
-        pack_pair_tiles(src, 2, F, D, packed);
-        rc = upload(L.pair_hi, packed.data(), packed.size());
-        if (rc == FFNRM_OK) rc = upload_scales(L.beta, beta, F, G, L.scales_half);
-    }
-    if (rc == FFNRM_OK) rc = upload_scales(L.alpha, alpha, F, G, L.scales_half);
-    if (rc == FFNRM_OK && ctx->cfg.max_tokens > std::min(ctx->gemv_tokens, ffnrm::kGemvMaxTokens)) {
-        const uint8_t *src[2] = {lo[0].data(), lo[1].data()};
-        pack_codes8(src, F, D, packed);
-        rc = upload(L.codes8, packed.data(), packed.size());
-        if (rc == FFNRM_OK &&
-            !make_u8_map(&L.codes8_map, L.codes8.ptr, uint64_t(D), uint64_t((F + 63) / 64 * 128), 128))
+    if (rc == FFNRM_OK && r != 2 && (rc = dev_alloc(L.plane, size_t(recs) * 8)) == FFNRM_OK)
+        ffnrm::pack_plane_kernel<<<pack_blocks(recs), 256>>>(lo[0], lo[1], r == 1 ? 0 : 2, F, D,
+                                                             static_cast<uint2 *>(L.plane.ptr));
+    if (rc == FFNRM_OK && L.has_fallback && (rc = dev_alloc(L.pair_hi, size_t(recs) * 16)) == FFNRM_OK)
+        ffnrm::pack_pair_kernel<<<pack_blocks(recs), 256>>>(full[0], full[1], 2, F, D, static_cast<uint4 *>(L.pair_hi.ptr));
+    const size_t sbytes = size_t(recs) * (L.scales_half ? 4 : 8);
+    if (rc == FFNRM_OK && (rc = dev_alloc(L.alpha, sbytes)) == FFNRM_OK)
+        ffnrm::pack_scales_kernel<<<pack_blocks(recs), 256>>>(static_cast<const float *>(alpha[0].dev),
+                                                              static_cast<const float *>(alpha[1].dev), F, G,
+                                                              L.scales_half, L.alpha.ptr);
+    if (rc == FFNRM_OK && L.has_fallback && (rc = dev_alloc(L.beta, sbytes)) == FFNRM_OK)
+        ffnrm::pack_scales_kernel<<<pack_blocks(recs), 256>>>(static_cast<const float *>(beta[0].dev),
+                                                              static_cast<const float *>(beta[1].dev), F, G,
+                                                              L.scales_half, L.beta.ptr);
+    if (rc == FFNRM_OK && ctx->res_kernel == 1 && ctx->cfg.max_tokens > std::min(ctx->gemv_tokens, ffnrm::kGemvMaxTokens) &&
+        (rc = dev_alloc(L.codes8, size_t(F64) * 128 * D)) == FFNRM_OK) {
+        ffnrm::pack_codes8_kernel<<<pack_blocks(F64 * 128 * D / 16), 256>>>(lo[0], lo[1], F, D,
+                                                                             static_cast<uint4 *>(L.codes8.ptr));
+        if (!make_u8_map(&L.codes8_map, L.codes8.ptr, uint64_t(D), uint64_t(F64 * 128), 128))
             rc = fail(FFNRM_ERR_CUDA, "cuTensorMapEncodeTiled rejected the byte codes");
     }
-    if (rc == FFNRM_OK) rc = upload_down(L.down, w->down, w->down_ld, F, D);
-    if (rc == FFNRM_OK && !make_fp16_map(&L.down_map, L.down.ptr, uint64_t((F + 15) / 16 * 16), uint64_t(D),
-                                         uint64_t((F + 15) / 16 * 16), 128))
+    // fp16 down [D, ld] (F used columns) -> row-major [D][F16] with zero columns F..F16-1
+    const int64_t F16 = (F + 15) / 16 * 16;
+    if (rc == FFNRM_OK && (rc = dev_alloc(L.down, size_t(D * F16) * 2)) == FFNRM_OK) {
+        FFNRM_CUDA(cudaMemset(L.down.ptr, 0, L.down.bytes));
+        FFNRM_CUDA(cudaMemcpy2D(L.down.ptr, size_t(F16) * 2, w->down, size_t(w->down_ld) * 2, size_t(F) * 2, size_t(D),
+                                cudaMemcpyDefault));
+    }
+    if (rc == FFNRM_OK && !make_fp16_map(&L.down_map, L.down.ptr, uint64_t(F16), uint64_t(D), uint64_t(F16), 128))
         rc = fail(FFNRM_ERR_CUDA, "cuTensorMapEncodeTiled rejected the down weight");
+    if (rc == FFNRM_OK) {
+        const cudaError_t e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) rc = fail(FFNRM_ERR_CUDA, "layer packing failed: %s", cudaGetErrorString(e));
+    }
     if (rc) {
         free_layer(L);
         return rc;

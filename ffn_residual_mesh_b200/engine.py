@@ -104,12 +104,24 @@ class ResidualMesh:
 
     # -- weights ------------------------------------------------------------
     def load_layer(self, layer: int, spec: LayerSpec) -> None:
+        """Copy one layer's weights into HBM in the device layouts. Arrays may be host
+        numpy arrays or torch tensors (host or on this context's device); the library
+        decodes and packs them on the GPU."""
         F, D, G = self.d_ff, self.d_model, self.groups
         keep = []
 
         def arr(a, dtype, shape=None):
             if a is None:
                 return None
+            if hasattr(a, "data_ptr"):  # torch tensor: used in place
+                import torch
+                want = {np.uint8: torch.uint8, np.float32: torch.float32}[dtype]
+                if a.dtype != want or not a.is_contiguous():
+                    raise ValueError(f"expected a contiguous {want} tensor, got {a.dtype}")
+                if shape is not None and tuple(a.shape) != shape:
+                    raise ValueError(f"expected shape {shape}, got {tuple(a.shape)}")
+                keep.append(a)
+                return a.data_ptr()
             v = np.ascontiguousarray(a, dtype=dtype)
             if shape is not None and v.shape != shape:
                 raise ValueError(f"expected shape {shape}, got {v.shape}")
@@ -125,19 +137,31 @@ class ResidualMesh:
         codes = [arr(spec.gate_codes, np.uint8, cshape), arr(spec.up_codes, np.uint8, cshape)]
         if spec.codes_format == N.CODES_BITPLANES:
             for a in (spec.gate_codes, spec.up_codes):
-                if np.asarray(a).size != self.r * F * D // 8:
+                size = a.numel() if hasattr(a, "numel") else np.asarray(a).size
+                if size != self.r * F * D // 8:
                     raise ValueError("bitplane payload length does not match d_ff, d_model and residual_bits")
-        down = np.asarray(spec.down)
-        if down.dtype != np.float16 or down.ndim != 2 or down.shape[0] != D or down.shape[1] < F:
-            raise ValueError(f"down must be fp16 [{D}, >= {F}], got {down.dtype} {down.shape}")
-        down = np.ascontiguousarray(down)
-        keep.append(down)
+        down = spec.down
+        if hasattr(down, "data_ptr"):
+            import torch
+            if down.dtype != torch.float16 or down.dim() != 2 or down.shape[0] != D or down.shape[1] < F \
+                    or down.stride(1) != 1:
+                raise ValueError(f"down must be fp16 [{D}, >= {F}] with unit column stride, got {down.dtype} "
+                                 f"{tuple(down.shape)}")
+            down_ptr, down_ld = down.data_ptr(), down.stride(0)
+            keep.append(down)
+        else:
+            down = np.asarray(down)
+            if down.dtype != np.float16 or down.ndim != 2 or down.shape[0] != D or down.shape[1] < F:
+                raise ValueError(f"down must be fp16 [{D}, >= {F}], got {down.dtype} {down.shape}")
+            down = np.ascontiguousarray(down)
+            keep.append(down)
+            down_ptr, down_ld = down.ctypes.data, down.shape[1]
         w = N.LayerWeights(
             spec.codes_format, codes[0], codes[1],
             arr(spec.gate_high, np.uint8), arr(spec.up_high, np.uint8),
             arr(spec.gate_alpha, np.float32, (F, G)), arr(spec.up_alpha, np.float32, (F, G)),
             arr(spec.gate_beta, np.float32, (F, G)), arr(spec.up_beta, np.float32, (F, G)),
-            down.ctypes.data, down.shape[1], int(spec.keep_fallback))
+            down_ptr, down_ld, int(spec.keep_fallback))
         N.check(self.lib.ffnrm_load_layer(self.handle, layer, ctypes.byref(w)))
 
     def layer_bytes(self, layer: int) -> tuple[int, int]:

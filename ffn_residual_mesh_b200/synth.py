@@ -100,10 +100,12 @@ def flagged_tiles(seed: int, n_tiles: int, fraction: float) -> np.ndarray:
     return mask
 
 
-def make_layer_device(seed: int, d_ff: int, d_model: int, rows: slice | None = None, device="cuda") -> LayerData:
+def make_layer_device(seed: int, d_ff: int, d_model: int, rows: slice | None = None, device="cuda",
+                      on_device: bool = False) -> LayerData:
     """Same distributions as :func:`make_layer`, drawn with torch's seeded CUDA
-    generator (fast for full-size stacks); returns host numpy arrays. Every rank
-    draws the full layer and keeps its shard, so shards of one seed agree."""
+    generator (fast for full-size stacks); returns host numpy arrays, or the torch
+    tensors on the device with ``on_device``. Every rank draws the full layer and keeps
+    its shard, so shards of one seed agree."""
     import torch
     gen = torch.Generator(device=device)
     gen.manual_seed(seed)
@@ -118,6 +120,9 @@ def make_layer_device(seed: int, d_ff: int, d_model: int, rows: slice | None = N
     ga, ua, gb, ub = scales(), scales(), -scales(), -scales()
     down = (torch.randn(d_model, d_ff, generator=gen, device=device) * 0.02).half()
     rows = rows or slice(0, d_ff)
+    if on_device:
+        cut = lambda t: t[rows].contiguous()
+        return LayerData(cut(gate), cut(up), cut(ga), cut(ua), cut(gb), cut(ub), down[:, rows].contiguous())
     host = lambda t: t[rows].contiguous().cpu().numpy()
     return LayerData(host(gate), host(up), host(ga), host(ua), host(gb), host(ub),
                      down[:, rows].contiguous().cpu().numpy())

@@ -82,11 +82,14 @@ typedef struct {
 int ffnrm_create(ffnrm_ctx **out, int device, const ffnrm_config *cfg);
 int ffnrm_destroy(ffnrm_ctx *ctx);
 
-/* Copy one layer's weights (host pointers, borrowed for the call) into HBM.
+/* Copy one layer's weights into HBM. Each array may be host memory or device memory of
+ * the context's device (borrowed for the call); host arrays are copied to the device
+ * first, and the artifact formats are decoded and packed into the device layouts by
+ * kernels. Synchronous: the call returns when the layer is ready.
  * Replaces load_projection (src/exact_residual_cuda_runner.cu:88-120) and the
  * resident fp16 down upload (src/exact_cpu_base_gpu_full_ffn_runner.cu:375-387).
  * alpha/beta are kept as fp16 on the device when every value is fp16-exact
- * (lossless), else as f32. */
+ * (lossless), else as f32. Q4 codes above 15 are rejected (FFNRM_ERR_ARG). */
 int ffnrm_load_layer(ffnrm_ctx *ctx, int layer, const ffnrm_layer_weights *w);
 
 /* Residual gate/up contraction. Replaces residual_kernel

@@ -183,13 +183,13 @@ def group_dots(codes: np.ndarray, z: np.ndarray) -> np.ndarray:
     c = np.asarray(codes, dtype=np.uint8)
     F = c.shape[0]
     c = c.reshape(F, -1, GROUP)
-    zz = np.asarray(z, dtype=np.int8).reshape(-1, c.shape[1], GROUP)
-    cf = c.astype(np.float64)
-    out = np.empty((zz.shape[0], F, c.shape[1]), dtype=np.int32)
-    for t in range(zz.shape[0]):
-        # float64 einsum is exact here: |P| <= 32*15*128 < 2**53.
-        out[t] = np.rint(np.einsum("rgi,gi->rg", cf, zz[t].astype(np.float64))).astype(np.int32)
-    return out
+    G = c.shape[1]
+    zz = np.asarray(z, dtype=np.int8).reshape(-1, G, GROUP)
+    # one [F, 32] x [32, T] product per group, in float64: exact, |P| <= 32*15*128 < 2**53
+    cg = np.ascontiguousarray(c.transpose(1, 0, 2)).astype(np.float64)   # [G, F, 32]
+    zg = np.ascontiguousarray(zz.transpose(1, 2, 0)).astype(np.float64)  # [G, 32, T]
+    prod = np.matmul(cg, zg)                                             # [G, F, T]
+    return np.rint(prod).astype(np.int32).transpose(2, 1, 0).copy()      # [T, F, G]
 
 
 def group_sums(z: np.ndarray) -> np.ndarray:
@@ -248,6 +248,48 @@ def full_projection(codes: np.ndarray, alpha, beta, z, s) -> np.ndarray:
     return scaled_projection(group_dots(codes, z), z, s, alpha, beta, 1)
 
 
+def dequant_projection(codes: np.ndarray, alpha, beta, z, s, code_multiplier: int = 1) -> np.ndarray:
+    """``out[t, row] = sum_k mult*codes[row,k]*alpha[row,k/32]*z[t,k]*s[t,k/32]`` (+ the beta term).
+
+    The per-element form of the same sum, as the reference's ``residual_kernel``
+    evaluates it (``q * alpha * z * scale`` per code,
+    ``src/exact_residual_cuda_runner.cu:141-143``), here as one float64 GEMM so that
+    full-size layers check in seconds. Every product ``alpha*q*s*z`` is exact in
+    float64 (at most 45 significant bits); only the float64 summation rounds.
+    ``beta`` adds ``sum_g s[t,g]*beta[row,g]*zsum[t,g]`` (``projection_from_group_dots``,
+    ``scripts/benchmark_exact_radix_split_pipeline.py:112-129``).
+    """
+    c = np.asarray(codes, dtype=np.uint8)
+    F, D = c.shape[0], c.size // c.shape[0]
+    G = D // GROUP
+    w = (c.reshape(F, G, GROUP).astype(np.float64) * np.asarray(alpha, np.float64)[:, :, None] *
+         code_multiplier).reshape(F, D)
+    zz = np.asarray(z, dtype=np.int8).reshape(-1, G, GROUP)
+    ss = np.asarray(s, dtype=np.float64).reshape(zz.shape[0], G)
+    x = (zz.astype(np.float64) * ss[:, :, None]).reshape(zz.shape[0], D)
+    out = x @ w.T
+    if beta is not None:
+        out += (ss * group_sums(z).astype(np.float64)) @ np.asarray(beta, np.float64).T
+    return out
+
+
+def residual_fast(codes, alpha, z, s, residual_bits: int) -> np.ndarray:
+    """:func:`residual` through :func:`dequant_projection` (same sum, float64 GEMM)."""
+    _, q_lo = split_codes(codes, residual_bits)
+    return dequant_projection(q_lo, alpha, None, z, s)
+
+
+def host_base_fast(codes, alpha, beta, z, s, residual_bits: int) -> np.ndarray:
+    """:func:`host_base` through :func:`dequant_projection` (same sum, float64 GEMM)."""
+    q_hi, _ = split_codes(codes, residual_bits)
+    return dequant_projection(q_hi, alpha, beta, z, s, 1 << residual_bits)
+
+
+def full_projection_fast(codes, alpha, beta, z, s) -> np.ndarray:
+    """:func:`full_projection` through :func:`dequant_projection`."""
+    return dequant_projection(codes, alpha, beta, z, s)
+
+
 def swiglu(g: np.ndarray, u: np.ndarray) -> np.ndarray:
     """``h = g / (1 + exp(-g)) * u`` (``benchmark_cpu_base_gpu_full_ffn.py:369``;
     ``exact_cpu_base_gpu_full_ffn_runner.cu:225-227``)."""
@@ -273,27 +315,30 @@ def tile_rows_mask(fallback_tiles: np.ndarray | None, F: int, tile_rows: int) ->
 
 def ffn_forward(gate_codes, up_codes, gate_alpha, up_alpha, gate_beta, up_beta, down_f16,
                 z, s, residual_bits: int, gate_base=None, up_base=None,
-                fallback_tiles=None, tile_rows: int = 256) -> dict:
+                fallback_tiles=None, tile_rows: int = 256, fast: bool = False) -> dict:
     """The full split path: merge base+residual before SwiGLU, then fp16 down.
 
     ``g = g_base + g_res``, ``u = u_base + u_res``, ``h = SiLU(g)*u``, ``y = h @ down.T``
     (``src/exact_cpu_base_gpu_full_ffn_runner.cu:217-240``;
     ``scripts/benchmark_cpu_base_gpu_full_ffn.py:360-371``). Rows in flagged tiles
     take the unsplit projection instead of base+residual. When no base is given
-    the host base is computed here. Returns float64 intermediates.
+    the host base is computed here. Returns float64 intermediates. ``fast`` evaluates
+    the same sums through :func:`dequant_projection` (large shapes).
     """
+    hb, rs, fp = (host_base_fast, residual_fast, full_projection_fast) if fast else (host_base, residual,
+                                                                                     full_projection)
     if gate_base is None:
-        gate_base = host_base(gate_codes, gate_alpha, gate_beta, z, s, residual_bits)
+        gate_base = hb(gate_codes, gate_alpha, gate_beta, z, s, residual_bits)
     if up_base is None:
-        up_base = host_base(up_codes, up_alpha, up_beta, z, s, residual_bits)
-    g_res = residual(gate_codes, gate_alpha, z, s, residual_bits)
-    u_res = residual(up_codes, up_alpha, z, s, residual_bits)
+        up_base = hb(up_codes, up_alpha, up_beta, z, s, residual_bits)
+    g_res = rs(gate_codes, gate_alpha, z, s, residual_bits)
+    u_res = rs(up_codes, up_alpha, z, s, residual_bits)
     g = np.asarray(gate_base, dtype=np.float64) + g_res
     u = np.asarray(up_base, dtype=np.float64) + u_res
     F = g.shape[1]
     flagged = tile_rows_mask(fallback_tiles, F, tile_rows)
     if flagged.any():
-        g[:, flagged] = full_projection(gate_codes[flagged], gate_alpha[flagged], gate_beta[flagged], z, s)
-        u[:, flagged] = full_projection(up_codes[flagged], up_alpha[flagged], up_beta[flagged], z, s)
+        g[:, flagged] = fp(gate_codes[flagged], gate_alpha[flagged], gate_beta[flagged], z, s)
+        u[:, flagged] = fp(up_codes[flagged], up_alpha[flagged], up_beta[flagged], z, s)
     h = swiglu(g, u)
     return {"gate_res": g_res, "up_res": u_res, "g": g, "u": u, "h": h, "y": down_projection(h, down_f16)}

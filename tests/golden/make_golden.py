@@ -2,7 +2,7 @@
 
 Run in a container that has the reference checkout (it is not needed at test time):
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <reference checkout> [--only NAME ...]
 
 Every value stored as an expected output is computed by a function imported from
 the reference's ``scripts/`` directory, never by this repository's oracle:
@@ -40,6 +40,8 @@ CASES = {
     "c4_decode_t32_r2": (128, 512, 32, 2, 0.0, 404, 64, ()),
     "c5_t5_r3_fallback": (200, 256, 5, 3, 0.0, 505, 64, (1, 3)),
     "c5_t3_r2_fallback": (130, 256, 3, 2, 0.0, 506, 32, (0, 4)),
+    # full 70B-class d_model, rows cut to 64, one flagged tile
+    "c4_d8192_t16_r2_fallback": (64, 8192, 16, 2, 0.0, 408, 32, (1,)),
 }
 
 
@@ -59,7 +61,8 @@ def synth(F, D, T, outliers, seed):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    ap.add_argument("--reference", type=Path, required=True, help="the reference checkout (its scripts/ are imported)")
+    ap.add_argument("--only", nargs="*", default=None, help="generate only these cases (and skip the KAT file)")
     args = ap.parse_args()
     sys.path.insert(0, str(args.reference / "scripts"))
     import torch
@@ -72,6 +75,20 @@ def main() -> None:
     from scan_q4k_host_base_gpu_residual import host_gpu_replay
 
     # Known-answer vectors taken from the reference's unit tests.
+    if args.only is None:
+        write_kats(quantize_groupwise_q8, pack_2bit_rows, pack_row_codes, compile_radix_table,
+                   evaluate_radix_table, encode_signed_base4_states)
+
+    for name, (F, D, T, r, outliers, seed, tile_rows, flagged) in CASES.items():
+        if args.only is not None and name not in args.only:
+            continue
+        make_case(name, F, D, T, r, outliers, seed, tile_rows, flagged, torch, compile_radix_table, direct_group_dots,
+                  encode_signed_base4_states, evaluate_radix_table, pack_bitplanes, pack_row_codes, host_gpu_replay,
+                  projection_from_group_dots, quantize_groupwise_q8)
+
+
+def write_kats(quantize_groupwise_q8, pack_2bit_rows, pack_row_codes, compile_radix_table, evaluate_radix_table,
+               encode_signed_base4_states):
     kat_x = np.array([[-1.0, -0.5, 0.0, 1.0, -2.0, 0.0, 1.0, 2.0]], dtype=np.float32)
     kat_z, kat_s = quantize_groupwise_q8(kat_x, group_size=4)
     kat_codes = np.array([[0, 1, 2, 3, 3, 2, 1, 0]], dtype=np.uint8)
@@ -86,57 +103,60 @@ def main() -> None:
                         pack_bytes_v2=pack_row_codes(kat_codes, bits=2),
                         radix_q_hi=q_hi_kat, radix_z=z_kat, radix_dots=radix_dots)
 
-    for name, (F, D, T, r, outliers, seed, tile_rows, flagged) in CASES.items():
-        codes, alpha, beta, x, down = synth(F, D, T, outliers, seed)
-        z, s = quantize_groupwise_q8(x, group_size=32)
-        G = D // 32
-        q_hi, q_lo = codes >> r, codes & ((1 << r) - 1)
-        grouped = lambda c: c.reshape(F, G, 32)
-        p_lo = np.stack([direct_group_dots(grouped(q_lo), z[t]) for t in range(T)]).astype(np.int32)
-        p_hi = np.stack([direct_group_dots(grouped(q_hi), z[t]) for t in range(T)]).astype(np.int32)
-        p_full = np.stack([direct_group_dots(grouped(codes), z[t]) for t in range(T)]).astype(np.int32)
-        # Batched split through the reference's host/GPU replay on dequantised activations.
-        xq = torch.from_numpy((z.reshape(T, G, 32).astype(np.float32) * s[:, :, None]).reshape(T, D))
-        blocks = D // 256
-        host, res, merged = host_gpu_replay(xq, codes.reshape(F, blocks, 256),
-                                            alpha.reshape(F, blocks, 8), beta.reshape(F, blocks, 8), r)
-        full = np.stack([projection_from_group_dots(direct_group_dots(grouped(codes), z[t]), z[t:t + 1],
-                                                    s[t:t + 1], alpha, beta, 1) for t in range(T)])
-        # Second projection (up) from the same law with a shifted seed.
-        codes_u, alpha_u, beta_u, _, _ = synth(F, D, T, 0.0, seed + 7)
-        host_u, res_u, merged_u = host_gpu_replay(xq, codes_u.reshape(F, blocks, 256),
-                                                  alpha_u.reshape(F, blocks, 8), beta_u.reshape(F, blocks, 8), r)
-        full_u = np.stack([projection_from_group_dots(direct_group_dots(grouped(codes_u), z[t]), z[t:t + 1],
-                                                      s[t:t + 1], alpha_u, beta_u, 1) for t in range(T)])
-        g = merged.double().numpy()
-        u = merged_u.double().numpy()
-        rows = np.zeros(F, dtype=bool)
-        for tile in flagged:
-            rows[tile * tile_rows:(tile + 1) * tile_rows] = True
-        g[:, rows] = full[:, rows]
-        u[:, rows] = full_u[:, rows]
-        hidden = g / (1.0 + np.exp(-g)) * u  # benchmark_cpu_base_gpu_full_ffn.py:369
-        y = hidden @ down.astype(np.float64).T  # :370
-        extra = {}
-        if r == 2:
-            extra["qlo2_rowpacked"] = pack_row_codes(q_lo, bits=2)
-            extra["qlo2_rowpacked_up"] = pack_row_codes(codes_u & 3, bits=2)
-            if T == 1:
-                table, high_sum = compile_radix_table(grouped(q_hi), block_size=4)
-                states = encode_signed_base4_states(z[0], block_size=4)
-                radix_hi = evaluate_radix_table(table, high_sum, states, blocks_per_group=8)
-                extra["radix_p_hi"] = radix_hi
-                extra["radix_base"] = projection_from_group_dots(radix_hi, z, s, alpha, beta, code_multiplier=4)
-        extra["lo_bitplanes"] = np.frombuffer(pack_bitplanes(q_lo, r), dtype=np.uint8)
-        extra["hi_bitplanes"] = np.frombuffer(pack_bitplanes(q_hi, 4 - r), dtype=np.uint8)
-        np.savez_compressed(
-            HERE / f"{name}.npz", F=F, D=D, T=T, r=r, tile_rows=tile_rows, flagged=np.array(flagged, dtype=np.int32),
-            codes=codes, alpha=alpha, beta=beta, codes_up=codes_u, alpha_up=alpha_u, beta_up=beta_u,
-            x=x, z=z, s=s, down=down, p_lo=p_lo, p_hi=p_hi, p_full=p_full,
-            host=host.numpy(), res=res.numpy(), merged=merged.numpy(), full=full,
-            host_up=host_u.numpy(), res_up=res_u.numpy(), merged_up=merged_u.numpy(), full_up=full_u,
-            g=g, u=u, h=hidden, y=y, **extra)
-        print(name, "ok")
+
+def make_case(name, F, D, T, r, outliers, seed, tile_rows, flagged, torch, compile_radix_table, direct_group_dots,
+              encode_signed_base4_states, evaluate_radix_table, pack_bitplanes, pack_row_codes, host_gpu_replay,
+              projection_from_group_dots, quantize_groupwise_q8):
+    codes, alpha, beta, x, down = synth(F, D, T, outliers, seed)
+    z, s = quantize_groupwise_q8(x, group_size=32)
+    G = D // 32
+    q_hi, q_lo = codes >> r, codes & ((1 << r) - 1)
+    grouped = lambda c: c.reshape(F, G, 32)
+    p_lo = np.stack([direct_group_dots(grouped(q_lo), z[t]) for t in range(T)]).astype(np.int32)
+    p_hi = np.stack([direct_group_dots(grouped(q_hi), z[t]) for t in range(T)]).astype(np.int32)
+    p_full = np.stack([direct_group_dots(grouped(codes), z[t]) for t in range(T)]).astype(np.int32)
+    # Batched split through the reference's host/GPU replay on dequantised activations.
+    xq = torch.from_numpy((z.reshape(T, G, 32).astype(np.float32) * s[:, :, None]).reshape(T, D))
+    blocks = D // 256
+    host, res, merged = host_gpu_replay(xq, codes.reshape(F, blocks, 256),
+                                        alpha.reshape(F, blocks, 8), beta.reshape(F, blocks, 8), r)
+    full = np.stack([projection_from_group_dots(direct_group_dots(grouped(codes), z[t]), z[t:t + 1],
+                                                s[t:t + 1], alpha, beta, 1) for t in range(T)])
+    # Second projection (up) from the same law with a shifted seed.
+    codes_u, alpha_u, beta_u, _, _ = synth(F, D, T, 0.0, seed + 7)
+    host_u, res_u, merged_u = host_gpu_replay(xq, codes_u.reshape(F, blocks, 256),
+                                              alpha_u.reshape(F, blocks, 8), beta_u.reshape(F, blocks, 8), r)
+    full_u = np.stack([projection_from_group_dots(direct_group_dots(grouped(codes_u), z[t]), z[t:t + 1],
+                                                  s[t:t + 1], alpha_u, beta_u, 1) for t in range(T)])
+    g = merged.double().numpy()
+    u = merged_u.double().numpy()
+    rows = np.zeros(F, dtype=bool)
+    for tile in flagged:
+        rows[tile * tile_rows:(tile + 1) * tile_rows] = True
+    g[:, rows] = full[:, rows]
+    u[:, rows] = full_u[:, rows]
+    hidden = g / (1.0 + np.exp(-g)) * u  # benchmark_cpu_base_gpu_full_ffn.py:369
+    y = hidden @ down.astype(np.float64).T  # :370
+    extra = {}
+    if r == 2:
+        extra["qlo2_rowpacked"] = pack_row_codes(q_lo, bits=2)
+        extra["qlo2_rowpacked_up"] = pack_row_codes(codes_u & 3, bits=2)
+        if T == 1:
+            table, high_sum = compile_radix_table(grouped(q_hi), block_size=4)
+            states = encode_signed_base4_states(z[0], block_size=4)
+            radix_hi = evaluate_radix_table(table, high_sum, states, blocks_per_group=8)
+            extra["radix_p_hi"] = radix_hi
+            extra["radix_base"] = projection_from_group_dots(radix_hi, z, s, alpha, beta, code_multiplier=4)
+    extra["lo_bitplanes"] = np.frombuffer(pack_bitplanes(q_lo, r), dtype=np.uint8)
+    extra["hi_bitplanes"] = np.frombuffer(pack_bitplanes(q_hi, 4 - r), dtype=np.uint8)
+    np.savez_compressed(
+        HERE / f"{name}.npz", F=F, D=D, T=T, r=r, tile_rows=tile_rows, flagged=np.array(flagged, dtype=np.int32),
+        codes=codes, alpha=alpha, beta=beta, codes_up=codes_u, alpha_up=alpha_u, beta_up=beta_u,
+        x=x, z=z, s=s, down=down, p_lo=p_lo, p_hi=p_hi, p_full=p_full,
+        host=host.numpy(), res=res.numpy(), merged=merged.numpy(), full=full,
+        host_up=host_u.numpy(), res_up=res_u.numpy(), merged_up=merged_u.numpy(), full_up=full_u,
+        g=g, u=u, h=hidden, y=y, **extra)
+    print(name, "ok")
 
 
 if __name__ == "__main__":

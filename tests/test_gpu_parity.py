@@ -16,7 +16,7 @@ from oracle import ffnrm_oracle as O
 pytestmark = pytest.mark.gpu
 
 CASES = ["c1_decode_t1_r2", "c2_decode_t8_r2", "c3_decode_t16_r1_outliers", "c4_decode_t32_r2",
-         "c5_t5_r3_fallback", "c5_t3_r2_fallback"]
+         "c4_d8192_t16_r2_fallback", "c5_t5_r3_fallback", "c5_t3_r2_fallback"]
 Y_MAX_ABS, Y_REL_L2 = 1e-2, 1e-3
 
 
@@ -350,8 +350,8 @@ def test_eager_call_after_capture(cuda):
 @pytest.mark.parametrize("T,F,r,half_alpha", [(5, 200, 2, True), (16, 64, 1, True), (17, 1000, 3, False),
                                               (64, 1000, 2, True), (100, 130, 2, False), (33, 333, 1, False)])
 def test_tensor_core_residual_tiles(T, F, r, half_alpha, cuda, monkeypatch):
-    """Batches of 5+ tokens without fallback tiles run on the tcgen05 kind::i8 tiles
-    (64 gate + 64 up rows x 16 or 32 tokens): group dots bit-exact against the oracle
+    """Batches of 3+ tokens run on the tcgen05 kind::i8 tiles over the packed records
+    (64 gate + 64 up rows x 16..128 tokens): group dots bit-exact against the oracle
     and against the mma.sync tiles, residuals and the forward output within tolerance,
     for r = 1/2/3, fp16-exact and f32 alpha, ragged d_ff and partial token tiles."""
     import torch
@@ -367,8 +367,8 @@ def test_tensor_core_residual_tiles(T, F, r, half_alpha, cuda, monkeypatch):
     ub = O.host_base(L.up_codes, L.up_alpha, L.up_beta, z, s, r)
     spec = LayerSpec(L.gate_codes, L.up_codes, L.gate_alpha, L.up_alpha, L.down, L.gate_beta, L.up_beta)
     results = {}
-    for legacy in ("0", "1"):
-        monkeypatch.setenv("FFNRM_RESIDUAL_MMA_SYNC", legacy)
+    for legacy in ("packed", "mma"):
+        monkeypatch.setenv("FFNRM_RESIDUAL_KERNEL", legacy)
         ctx = ResidualMesh(D, F, r, 1, T)
         ctx.load_layer(0, spec)
         g = torch.empty(T, F, device=cuda)
@@ -382,15 +382,15 @@ def test_tensor_core_residual_tiles(T, F, r, half_alpha, cuda, monkeypatch):
         ctx.check_device_error()
         results[legacy] = (dots.cpu().numpy(), g.cpu().numpy(), u.cpu().numpy(), y32.cpu().numpy())
         ctx.close()
-    dots, g, u, y = results["0"]
+    dots, g, u, y = results["packed"]
     mask = (1 << r) - 1
     np.testing.assert_array_equal(dots[0], O.group_dots(L.gate_codes & mask, z))
     np.testing.assert_array_equal(dots[1], O.group_dots(L.up_codes & mask, z))
-    np.testing.assert_array_equal(dots, results["1"][0])
+    np.testing.assert_array_equal(dots, results["mma"][0])
     close_rows(g, O.residual(L.gate_codes, L.gate_alpha, z, s, r), rtol=2e-5)
     close_rows(u, O.residual(L.up_codes, L.up_alpha, z, s, r), rtol=2e-5)
     ref = O.ffn_forward(L.gate_codes, L.up_codes, L.gate_alpha, L.up_alpha, L.gate_beta, L.up_beta, L.down, z, s, r,
                         gate_base=gb, up_base=ub)
     assert rel_l2(y, ref["y"]) < 1e-5
     assert np.abs(y - ref["y"]).max() < Y_MAX_ABS
-    assert rel_l2(y, results["1"][3]) < 1e-5
+    assert rel_l2(y, results["mma"][3]) < 1e-5
