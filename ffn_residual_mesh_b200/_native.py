@@ -41,6 +41,7 @@ SIGNATURES = {
     "ffnrm_check_device_error": (c_int, [c_void_p, c_void_p]),
     "ffnrm_down_project_noalloc": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int, c_int, c_int,
                                            c_void_p, c_void_p, c_void_p, c_void_p]),
+    "ffnrm_noalloc_status": (c_int, [c_void_p, c_void_p]),
     "ffnrm_profile_enable": (c_int, [c_void_p, c_int]),
     "ffnrm_profile_read": (c_int, [c_void_p, c_int, POINTER(ctypes.c_double), POINTER(c_int64)]),
     "ffnrm_last_error": (c_char_p, []),

@@ -590,28 +590,50 @@ int enqueue_down(ffnrm_ctx *ctx, int layer, int T, float *y32, uint16_t *y16, cu
 }
 
 // ---------------------------------------------------------------------------
-// Allocation-free down projection: scratch in file-scope device arrays
+// Allocation-free down projection: its only scratch is a file-scope device word
 // ---------------------------------------------------------------------------
-constexpr int kNoAllocMaxTokens = 256;
-constexpr int kNoAllocMaxDModel = 16384;
+constexpr int kNoAllocMaxTokens = 256;     // largest token-tile grid the call launches
+constexpr int kNoAllocMaxDModel = 16384;   // largest d_model (output row tiles) it accepts
 constexpr int kNoAllocMaxDevices = 64;
 
-// Held by every GPU that loads this library, until the process exits.
-__device__ __align__(256) int g_noalloc_status[64];
+// The default status word of calls that pass status = NULL. Every GPU that loads this
+// library holds its own copy until the process exits.
+__device__ __align__(256) int g_noalloc_status;
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext *);
+
+CUcontext current_context() {
+    static CtxGetCurrentFn fn = [] {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            ptr = nullptr;
+        return reinterpret_cast<CtxGetCurrentFn>(ptr);
+    }();
+    CUcontext c = nullptr;
+    if (fn) fn(&c);
+    return c;
+}
 
 struct NoAllocScratch {
     int *status = nullptr;
+    CUcontext ctx = nullptr;  // the context the address belongs to
 };
 std::mutex g_noalloc_mutex;
 NoAllocScratch g_noalloc[kNoAllocMaxDevices];
 
-// Device address of the status word on `dev` (the current device), looked up once.
+// Device address of the status word on `dev` (the current device). It is looked up with
+// cudaGetSymbolAddress the first time and again whenever the device's context changed (a
+// reset or a new primary context), so no stale address is ever used.
 int noalloc_scratch(int dev, NoAllocScratch &out) {
     std::lock_guard<std::mutex> lock(g_noalloc_mutex);
     NoAllocScratch &s = g_noalloc[dev];
-    if (!s.status) {
+    const CUcontext c = current_context();
+    if (!s.status || s.ctx != c) {
         NoAllocScratch t;
         FFNRM_CUDA(cudaGetSymbolAddress(reinterpret_cast<void **>(&t.status), g_noalloc_status));
+        t.ctx = c;
         s = t;
     }
     out = s;
@@ -1120,8 +1142,8 @@ int ffnrm_down_project_noalloc(const uint16_t *down, int64_t down_ld, const uint
                                int64_t h_ld, int d_model, int d_ff, int tokens, float *y_f32, uint16_t *y_f16,
                                int32_t *status, void *stream) {
     if (tokens < 0 || tokens > kNoAllocMaxTokens)
-        return fail(FFNRM_ERR_ARG, "tokens=%d outside [0, %d] (the scratch of the allocation-free call is fixed)",
-                    tokens, kNoAllocMaxTokens);
+        return fail(FFNRM_ERR_ARG, "tokens=%d outside [0, %d], the largest token-tile grid this call launches", tokens,
+                    kNoAllocMaxTokens);
     if (d_model <= 0 || d_model % 128 || d_model > kNoAllocMaxDModel)
         return fail(FFNRM_ERR_ARG, "d_model=%d must be a positive multiple of 128 up to %d", d_model,
                     kNoAllocMaxDModel);
@@ -1144,6 +1166,21 @@ int ffnrm_down_project_noalloc(const uint16_t *down, int64_t down_ld, const uint
     if (tokens <= 32) return launch_down_noalloc<32>(down, down_ld, h_hi, h_lo, h_ld, d_model, d_ff, tokens, y_f32, y_f16, status, scr, st);
     if (tokens <= 64) return launch_down_noalloc<64>(down, down_ld, h_hi, h_lo, h_ld, d_model, d_ff, tokens, y_f32, y_f16, status, scr, st);
     return launch_down_noalloc<128>(down, down_ld, h_hi, h_lo, h_ld, d_model, d_ff, tokens, y_f32, y_f16, status, scr, st);
+}
+
+int ffnrm_noalloc_status(int32_t *out, void *stream) {
+    if (!out) return fail(FFNRM_ERR_ARG, "null argument");
+    int dev = 0;
+    FFNRM_CUDA(cudaGetDevice(&dev));
+    if (dev >= kNoAllocMaxDevices) return fail(FFNRM_ERR_ARG, "device %d beyond the supported %d", dev, kNoAllocMaxDevices);
+    NoAllocScratch scr;
+    int rc = noalloc_scratch(dev, scr);
+    if (rc) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    FFNRM_CUDA(cudaMemcpyAsync(out, scr.status, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+    FFNRM_CUDA(cudaMemsetAsync(scr.status, 0, sizeof(int32_t), st));
+    FFNRM_CUDA(cudaStreamSynchronize(st));
+    return FFNRM_OK;
 }
 
 int ffnrm_check_device_error(ffnrm_ctx *ctx, void *stream) {

@@ -174,24 +174,30 @@ int ffnrm_layer_bytes(ffnrm_ctx *ctx, int layer, int64_t *residual_bytes, int64_
  * memory -- code running while a CUDA graph is being captured or inside a graph node,
  * allocators that forbid cudaMalloc on the serving path, or processes whose memory pool
  * is fully reserved. It needs no context and calls no cudaMalloc/cudaFree: split-K
- * partial sums are reduced across a thread-block cluster in shared memory, and the
- * only scratch, the default status word, is a fixed device array of this library,
+ * partial sums are reduced across a thread-block cluster in shared memory, and its only
+ * scratch, the default status word, is a file-scope device variable of this library,
  * which every GPU that loads the library holds until the process exits.
  * Device pointers: down fp16 [d_model][down_ld] row-major (d_ff used columns), h_hi and
  * h_lo fp16 [tokens][h_ld] whose sum is h (pass zeros as h_lo for plain fp16 h), outputs
  * y_f32 [tokens][d_model] (16-byte aligned) and/or y_f16 (8-byte aligned); status
  * (optional, 1 int) receives a nonzero code if the kernel gave up on a bounded pipeline
- * wait. Limits: tokens <= 256, d_model a multiple of 128 up to 16384, down/h 16-byte
- * aligned, down_ld and h_ld multiples of 8 and >= d_ff; larger requests return
- * FFNRM_ERR_ARG.
- * The first call on a device looks up the status word's device address
- * (cudaGetSymbolAddress); make that first call before any stream capture. Calls that
- * pass status = NULL share the default status word and clear it, so such calls that
- * overlap on the GPU (different streams, or another thread) race on it and must be
- * serialised by the caller (or pass their own status word). */
+ * wait. Limits (the largest tile grid the call launches): tokens <= 256, d_model a
+ * multiple of 128 up to 16384; down/h 16-byte aligned, down_ld and h_ld multiples of 8 and
+ * >= d_ff; other requests return FFNRM_ERR_ARG.
+ * The status word's device address is looked up (cudaGetSymbolAddress) on the first call
+ * on a device, and again after the device's context changed; make that first call before
+ * any stream capture. Calls with status = NULL share the default status word and clear it
+ * when they start, so such calls that overlap on the GPU (different streams, or another
+ * thread) race on it: serialise them, or pass a status word per call. A caller that passes
+ * NULL reads (and clears) the default word with ffnrm_noalloc_status. */
 int ffnrm_down_project_noalloc(const uint16_t *down, int64_t down_ld, const uint16_t *h_hi, const uint16_t *h_lo,
                                int64_t h_ld, int d_model, int d_ff, int tokens, float *y_f32, uint16_t *y_f16,
                                int32_t *status, void *stream);
+
+/* Copies the current device's default status word of ffnrm_down_project_noalloc (nonzero:
+ * a call with status = NULL gave up on a bounded wait) to *out and clears it, ordered on
+ * `stream`, and synchronises `stream`. Allocates nothing. */
+int ffnrm_noalloc_status(int32_t *out, void *stream);
 
 /* Synchronises `stream` and reports whether any kernel of this context gave up on a
  * bounded pipeline wait since the last check (FFNRM_ERR_TIMEOUT, error word cleared). */
