@@ -44,6 +44,11 @@ SIGNATURES = {
     "ffnrm_noalloc_status": (c_int, [c_void_p, c_void_p]),
     "ffnrm_profile_enable": (c_int, [c_void_p, c_int]),
     "ffnrm_profile_read": (c_int, [c_void_p, c_int, POINTER(ctypes.c_double), POINTER(c_int64)]),
+    "ffnrm_base_producer_create": (c_int, [POINTER(c_void_p), c_int]),
+    "ffnrm_base_producer_destroy": (c_int, [c_void_p]),
+    "ffnrm_base_from_table": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_int,
+                                      c_void_p, c_int64, c_void_p]),
+    "ffnrm_table_dots": (c_int, [c_void_p, c_void_p, c_void_p]),
     "ffnrm_last_error": (c_char_p, []),
     "ffnrm_version": (c_char_p, []),
 }

@@ -29,6 +29,7 @@
 #include "peer_reduce.cuh"
 #include "residual_tc.cuh"
 #include "residual_umma.cuh"
+#include "residual_prefill.cuh"
 
 namespace {
 
@@ -163,6 +164,7 @@ struct ffnrm_ctx {
     // (default); 0 = packed records only (no byte codes are built); 2 = mma.sync tiles
     // (FFNRM_RESIDUAL_KERNEL=bytes|packed|mma)
     int res_kernel = 1;
+    int prefill_tokens = 0;  // batches of at least this many tokens (no fallback tiles) take the prefill residual (0 = off)
     CUtensorMap h_map[4][2];             // h hi/lo views for token tiles 16, 32, 64, 128
     __half *h_hi = nullptr, *h_lo = nullptr;  // [Tm, F16] h = SiLU(g)*u as fp16 hi + lo
     // host-streamed mode staging, double-buffered per call
@@ -473,6 +475,83 @@ int launch_residual_umma_t(ffnrm_ctx *ctx, const LayerDev &L, ffnrm::ResidualPar
     return FFNRM_OK;
 }
 
+// Shared-memory layout of the prefill residual: ring depths chosen to fit one CTA per SM.
+// Activations (SA) and code records (S1) cover the L2/HBM latency (~4 K tiles each),
+// widened codes (SW) one K tile of widening ahead of the MMA, f32 alphas (S4) the lag
+// of the drain behind the widening (the MMA runs up to two groups ahead of the drain).
+ffnrm::PfLayout prefill_layout(bool has_pair, bool has_plane, bool alpha_half, size_t budget) {
+    using namespace ffnrm;
+    PfLayout L{}, best{};
+    L.pair_bytes = has_pair ? 4096 : 0;
+    L.plane_bytes = has_plane ? 2048 : 0;
+    L.alpha_bytes = alpha_half ? 1024 : 2048;
+    L.off_pair = 0;
+    L.off_plane = 2 * L.pair_bytes;
+    L.off_alpha = L.off_plane + 2 * L.plane_bytes;
+    L.src_bytes = L.off_alpha + 2 * L.alpha_bytes;
+    const int a = kPfTokens * kPfKTile, w = kPfN * kPfKTile, al = 4 * kPfN * 4;
+    const int bars = (2 * (kPfMaxSA + kPfMaxS1 + kPfMaxSW + kPfMaxS4) + 2 * 2 + 1) * 8 + 16;
+    best.total = -1;
+    int best_score = -1;
+    for (int SW = 2; SW <= 3; ++SW)
+        for (int SA = 2; SA <= kPfMaxSA; ++SA)
+            for (int S1 = 2; S1 <= kPfMaxS1; ++S1)
+                for (int S4 = 2; S4 <= kPfMaxS4; ++S4) {
+                    L.SA = SA;
+                    L.S1 = S1;
+                    L.SW = SW;
+                    L.S4 = S4;
+                    L.w_off = SA * a;
+                    L.src_off = L.w_off + SW * w;
+                    L.al_off = L.src_off + S1 * L.src_bytes;
+                    L.bar_off = (L.al_off + S4 * al + 7) / 8 * 8;
+                    L.total = L.bar_off + bars;
+                    if (size_t(L.total) + 1024 > budget) continue;
+                    const int score = 4 * std::min(SA, 4) + 4 * std::min(S1, 4) + 3 * std::min(S4, 4) + 2 * SW +
+                                      std::min(SA, 6) + std::min(S1, 6) + std::min(S4, 6) / 2;
+                    if (score > best_score || (score == best_score && L.total < best.total)) {
+                        best_score = score;
+                        best = L;
+                    }
+                }
+    return best;
+}
+
+template <bool DOTS>
+int launch_residual_prefill_t(ffnrm_ctx *ctx, const LayerDev &L, ffnrm::ResidualParams &p, cudaStream_t st) {
+    using namespace ffnrm;
+    PfParams P{};
+    P.rbits = ctx->cfg.residual_bits;
+    P.alpha_half = L.scales_half ? 1 : 0;
+    P.F64 = (p.F + 63) / 64;
+    const bool has_pair = P.rbits != 1;
+    if ((has_pair && !L.pair.ptr) || (P.rbits != 2 && !L.plane.ptr))
+        return fail(FFNRM_ERR_STATE, "layer lacks the code records the prefill residual reads");
+    P.L = prefill_layout(has_pair, P.rbits != 2, L.scales_half, 227 * 1024);
+    if (P.L.total < 0) return fail(FFNRM_ERR_ARG, "no shared-memory layout for the prefill residual");
+    const size_t smem = size_t(P.L.total) + 1024;
+    auto kern = residual_prefill_kernel<DOTS>;
+    // The warp-group register split (setmaxnreg) balances only at the launch register count
+    // it was designed for; any other count would leave the drain's request unsatisfiable.
+    cudaFuncAttributes fa{};
+    FFNRM_CUDA(cudaFuncGetAttributes(&fa, kern));
+    if (fa.numRegs != kPfRegsLaunch)
+        return fail(FFNRM_ERR_STATE, "prefill residual built with %d registers per thread, needs %d", fa.numRegs,
+                    kPfRegsLaunch);
+    CUtensorMap zm;
+    if (!make_z_map(&zm, p.z, uint64_t(p.D), uint64_t(p.T), kPfTokens))
+        return fail(FFNRM_ERR_CUDA, "cuTensorMapEncodeTiled rejected the activations");
+    FFNRM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+    p.row_blocks = (p.F + 31) / 32;
+    p.err = ctx->err;
+    P.p = p;
+    dim3 grid(unsigned((p.T + kPfTokens - 1) / kPfTokens), unsigned((p.F + kPfRows - 1) / kPfRows));
+    ProfScope prof(ctx, st, FFNRM_KERNEL_RESIDUAL);
+    FFNRM_CUDA(launch_dependent(kern, grid, dim3(kPfThreads), smem, st, true, 1, zm, P));
+    ctx->launches++;
+    return FFNRM_OK;
+}
+
 // T <= 2 (FFNRM_GEMV_TOKENS): dp4a GEMV on the packed records. Larger batches: tcgen05
 // kind::i8 tiles - on the byte codes (token tiles of 16 or 32) when the layer has them and
 // no fallback tile is flagged; otherwise, fallback tiles included, on the packed records
@@ -491,6 +570,9 @@ int launch_residual_rb(ffnrm_ctx *ctx, const LayerDev &L, ffnrm::ResidualParams 
         if (p.T <= 16) return launch_residual_mma_nt<RB, 2>(ctx, p, half, st);
         return launch_residual_mma_nt<RB, 4>(ctx, p, half, st);  // 32-token tiles (64 would spill)
     }
+    if (p.fallback_tiles == nullptr && ctx->prefill_tokens > 0 && p.T >= ctx->prefill_tokens &&
+        (reinterpret_cast<uintptr_t>(p.s) & 15) == 0)  // the prefill drain reads s as float4
+        return p.dots ? launch_residual_prefill_t<true>(ctx, L, p, st) : launch_residual_prefill_t<false>(ctx, L, p, st);
     if (ctx->res_kernel == 1 && p.fallback_tiles == nullptr && L.codes8.ptr &&
         ffnrm::ResTcCfg<32, false>::smem(p.G, 2) <= 227 * 1024) {
         if (p.T <= 16) return half ? launch_residual_tc_t<16, true>(ctx, L, p, st) : launch_residual_tc_t<16, false>(ctx, L, p, st);
@@ -576,6 +658,7 @@ int launch_down_t(ffnrm_ctx *ctx, const CUtensorMap &wmap, int map_idx, ffnrm::D
 
 int enqueue_down(ffnrm_ctx *ctx, int layer, int T, float *y32, uint16_t *y16, cudaStream_t st) {
     LayerDev &L = ctx->layers[size_t(layer)];
+    if (!L.down.ptr) return fail(FFNRM_ERR_STATE, "layer %d was loaded without a down projection", layer);
     ffnrm::DownUmmaParams p{};
     p.y32 = y32;
     p.y16 = reinterpret_cast<__half *>(y16);
@@ -666,6 +749,9 @@ int launch_down_noalloc(const uint16_t *down, int64_t down_ld, const uint16_t *h
 
 }  // namespace
 
+// Sets the calling thread's last error (used by the host-side translation units).
+int ffnrm_set_error(int code, const char *msg) { return fail(code, "%s", msg); }
+
 extern "C" {
 
 const char *ffnrm_last_error(void) { return g_last_error.c_str(); }
@@ -693,6 +779,7 @@ int ffnrm_create(ffnrm_ctx **out, int device, const ffnrm_config *cfg) {
     if (const char *e = std::getenv("FFNRM_RESIDUAL_KERNEL"))
         ctx->res_kernel = std::strcmp(e, "packed") == 0 ? 0 : std::strcmp(e, "mma") == 0 ? 2 : 1;
     if (const char *e = std::getenv("FFNRM_GEMV_TOKENS")) ctx->gemv_tokens = std::max(1, std::atoi(e));
+    if (const char *e = std::getenv("FFNRM_PREFILL_TOKENS")) ctx->prefill_tokens = std::max(0, std::atoi(e));
     cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
     const size_t TF = size_t(c.max_tokens) * c.d_ff, TD = size_t(c.max_tokens) * c.d_model;
     const size_t F16 = (size_t(c.d_ff) + 15) / 16 * 16;
@@ -755,12 +842,12 @@ int ffnrm_destroy(ffnrm_ctx *ctx) {
 int ffnrm_load_layer(ffnrm_ctx *ctx, int layer, const ffnrm_layer_weights *w) {
     if (!ctx || !w) return fail(FFNRM_ERR_ARG, "null argument");
     if (layer < 0 || layer >= ctx->cfg.n_layers) return fail(FFNRM_ERR_ARG, "layer %d out of range", layer);
-    if (!w->gate_codes || !w->up_codes || !w->gate_alpha || !w->up_alpha || !w->down)
-        return fail(FFNRM_ERR_ARG, "codes, alpha and down are required");
+    if (!w->gate_codes || !w->up_codes || !w->gate_alpha || !w->up_alpha)
+        return fail(FFNRM_ERR_ARG, "codes and alpha are required");
     const int64_t F = ctx->cfg.d_ff, D = ctx->cfg.d_model, G = ctx->G, n = F * D;
     const int r = ctx->cfg.residual_bits;
     const int fmt = w->codes_format;
-    if (w->down_ld < F) return fail(FFNRM_ERR_ARG, "down_ld=%lld must be >= d_ff=%lld", (long long)w->down_ld, (long long)F);
+    if (w->down && w->down_ld < F) return fail(FFNRM_ERR_ARG, "down_ld=%lld must be >= d_ff=%lld", (long long)w->down_ld, (long long)F);
     if (fmt != FFNRM_CODES_Q4_BYTES && fmt != FFNRM_CODES_QLO2_ROWPACKED && fmt != FFNRM_CODES_BITPLANES)
         return fail(FFNRM_ERR_ARG, "unknown codes_format %d", fmt);
     if (fmt == FFNRM_CODES_QLO2_ROWPACKED && r != 2)
@@ -846,12 +933,12 @@ int ffnrm_load_layer(ffnrm_ctx *ctx, int layer, const ffnrm_layer_weights *w) {
     }
     // fp16 down [D, ld] (F used columns) -> row-major [D][F16] with zero columns F..F16-1
     const int64_t F16 = (F + 15) / 16 * 16;
-    if (rc == FFNRM_OK && (rc = dev_alloc(L.down, size_t(D * F16) * 2)) == FFNRM_OK) {
+    if (rc == FFNRM_OK && w->down && (rc = dev_alloc(L.down, size_t(D * F16) * 2)) == FFNRM_OK) {
         FFNRM_CUDA(cudaMemset(L.down.ptr, 0, L.down.bytes));
         FFNRM_CUDA(cudaMemcpy2D(L.down.ptr, size_t(F16) * 2, w->down, size_t(w->down_ld) * 2, size_t(F) * 2, size_t(D),
                                 cudaMemcpyDefault));
     }
-    if (rc == FFNRM_OK && !make_fp16_map(&L.down_map, L.down.ptr, uint64_t(F16), uint64_t(D), uint64_t(F16), 128))
+    if (rc == FFNRM_OK && w->down && !make_fp16_map(&L.down_map, L.down.ptr, uint64_t(F16), uint64_t(D), uint64_t(F16), 128))
         rc = fail(FFNRM_ERR_CUDA, "cuTensorMapEncodeTiled rejected the down weight");
     if (rc == FFNRM_OK) {
         const cudaError_t e = cudaDeviceSynchronize();
@@ -888,6 +975,8 @@ int ffnrm_ffn_forward(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s
     if (tokens == 0) return FFNRM_OK;  // empty batch
     if (!z || !s || !gate_base || !up_base) return fail(FFNRM_ERR_ARG, "null device pointer");
     if (!y_f32 && !y_f16) return fail(FFNRM_ERR_ARG, "no output requested");
+    if (!ctx->layers[size_t(layer)].down.ptr)
+        return fail(FFNRM_ERR_STATE, "layer %d was loaded without a down projection", layer);
     if (!aligned(z, 16) || !aligned(s, 4) || !aligned(gate_base, 4) || !aligned(up_base, 4) || !aligned(y_f32, 16) ||
         !aligned(y_f16, 8))
         return fail(FFNRM_ERR_ARG, "z and y_f32 must be 16-byte aligned, y_f16 8-byte, s and base sums 4-byte");
@@ -907,6 +996,8 @@ int ffnrm_ffn_forward_host(ffnrm_ctx *ctx, int layer, const int8_t *z, const flo
     if ((rc = check_tokens(ctx, tokens))) return rc;
     if (tokens == 0) return FFNRM_OK;  // empty batch
     if (!z || !s || !gate_base || !up_base || !y_f16) return fail(FFNRM_ERR_ARG, "null host pointer");
+    if (!ctx->layers[size_t(layer)].down.ptr)
+        return fail(FFNRM_ERR_STATE, "layer %d was loaded without a down projection", layer);
     DeviceGuard guard(ctx->device);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int F = ctx->cfg.d_ff, D = ctx->cfg.d_model, G = ctx->G;

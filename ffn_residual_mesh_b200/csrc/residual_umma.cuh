@@ -65,7 +65,7 @@ constexpr int kUmMaxSB = 8;      // deepest activation ring
 
 template <int N>
 struct UmCfg {
-    static constexpr int DW = 2;                        // worker warps per TMEM lane quadrant
+    static constexpr int DW = N >= 64 ? 4 : 2;          // worker warps per TMEM lane quadrant
     static constexpr int workers = 128 * DW;            // worker threads (widen + drain)
     static constexpr int threads = 64 + workers;        // + producer warp + MMA warp
     static constexpr int a_bytes = 128 * kUmKTile;      // widened codes, 16 KB
@@ -346,6 +346,14 @@ __device__ __forceinline__ void residual_umma_body(const CUtensorMap &tm_z, cons
             float *dsz = sz_win + (w & 1) * kUmWin * Cfg::s_stride;
             for (int i = dt; i < ng * N; i += kUmDrain) {
                 const int tok = i / ng, g = i - tok * ng;
+                if (!cta_flagged) {
+                    // s alone: asynchronous copies, waited for at the next window barrier
+                    if (t0 + tok < p.T)
+                        sm100::cp_async4(dst + g * Cfg::s_stride + tok, p.s + int64_t(t0 + tok) * G + g0 + g);
+                    else
+                        dst[g * Cfg::s_stride + tok] = 0.f;
+                    continue;
+                }
                 float v = 0.f, vz = 0.f;
                 if (t0 + tok < p.T) {
                     v = __ldg(p.s + int64_t(t0 + tok) * G + g0 + g);
@@ -381,6 +389,7 @@ __device__ __forceinline__ void residual_umma_body(const CUtensorMap &tm_z, cons
             if (kt % (kUmWin / 4) == 0) {
                 // window kt/8 starts: its stores (one window earlier) become visible, and
                 // everyone is done with the window before it, whose buffer is refilled now
+                sm100::cp_async_wait_all();
                 asm volatile("bar.sync 1, %0;\n" ::"r"(kUmDrain) : "memory");
                 const int w = kt / (kUmWin / 4);
                 if (w + 1 < nwin) stage_window(w + 1);
@@ -409,7 +418,7 @@ __device__ __forceinline__ void residual_umma_body(const CUtensorMap &tm_z, cons
             // computed, and a buffer is released as soon as its last chunk has landed, so the
             // MMAs refill it while this warp still computes.
             constexpr int UPK = 4 / Cfg::gpb;                 // buffer uses per K tile
-            constexpr int CH = NH < 16 ? NH : (NH > 32 ? 16 : NH);  // columns per chunk
+            constexpr int CH = NH < 16 ? NH : 16;              // columns per chunk
             constexpr int CPG = NH / CH;                       // chunks per group
             constexpr int NCK = 4 * CPG;                       // chunks per K tile
             constexpr int NC = CH < 16 ? CH : 16;              // columns per TMEM load

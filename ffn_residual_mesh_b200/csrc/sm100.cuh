@@ -135,6 +135,17 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
           "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
 }
+// 32 lanes x 32 consecutive 32-bit TMEM columns -> 32 registers per thread.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
 
 // 32 lanes x 16 consecutive 32-bit TMEM columns <- 16 registers per thread.
@@ -201,6 +212,13 @@ __device__ __forceinline__ uint64_t smem_desc_plain(uint32_t addr, uint32_t lbo,
     return d;                // layout type 0: no swizzle
 }
 
+// 4-byte asynchronous copy global -> shared (cp.async, completion by cp_async_wait_all).
+__device__ __forceinline__ void cp_async4(void *smem_dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(smem_u32(smem_dst)), "l"(src) : "memory");
+}
+// Waits until every cp.async of this thread has landed in shared memory.
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
 // Make this thread's generic-proxy shared-memory writes visible to the async proxy
 // (tensor core operand reads).
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
@@ -210,28 +228,9 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
 }
 
 // Packed fp32 pair arithmetic (sm_100): d = a * b + c, d = a + b, d = a * b on float2.
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
-    float2 d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;\n"
-        : "=l"(reinterpret_cast<unsigned long long &>(d))
-        : "l"(reinterpret_cast<unsigned long long &>(a)), "l"(reinterpret_cast<unsigned long long &>(b)),
-          "l"(reinterpret_cast<unsigned long long &>(c)));
-    return d;
-}
-__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
-    float2 d;
-    asm("add.rn.f32x2 %0, %1, %2;\n"
-        : "=l"(reinterpret_cast<unsigned long long &>(d))
-        : "l"(reinterpret_cast<unsigned long long &>(a)), "l"(reinterpret_cast<unsigned long long &>(b)));
-    return d;
-}
-__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
-    float2 d;
-    asm("mul.rn.f32x2 %0, %1, %2;\n"
-        : "=l"(reinterpret_cast<unsigned long long &>(d))
-        : "l"(reinterpret_cast<unsigned long long &>(a)), "l"(reinterpret_cast<unsigned long long &>(b)));
-    return d;
-}
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
 
 // Shared-memory matrix descriptor for a K-major tile written by TMA with 128-byte
 // swizzle: rows of 128 B, 8-row (1024 B) swizzle atoms, so the stride between 8-row
@@ -253,6 +252,20 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t addr) {
 __host__ __device__ constexpr uint32_t umma_idesc_u8s8_s32(int M, int N) {
     return (2u << 4) | (0u << 7) | (1u << 10) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
 }
+
+// Instruction descriptor, kind::i8: A signed 8-bit (format 1), B unsigned 8-bit (format 0),
+// s32 accumulate, both K-major, M and N as given.
+__host__ __device__ constexpr uint32_t umma_idesc_s8u8_s32(int M, int N) {
+    return (2u << 4) | (1u << 7) | (0u << 10) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
+}
+
+// Warp-group register reallocation (all four warps of a warp group execute the same
+// instruction): lower this warp group's per-thread register count to R, or raise it to R
+// from the registers released by other warp groups of the CTA.
+template <int R>
+__device__ __forceinline__ void regs_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(R)); }
+template <int R>
+__device__ __forceinline__ void regs_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(R)); }
 
 // Instruction descriptor, kind::f16: A/B fp16 (format 0), f32 accumulate (c_format 1),
 // both K-major, M and N as given.

@@ -72,7 +72,8 @@ typedef struct {
     const float *up_alpha;
     const float *gate_beta;        /* [F, G] per-group weight min term; NULL = no fallback */
     const float *up_beta;
-    const uint16_t *down;          /* fp16 down weight, row o at down + o*down_ld, F columns */
+    const uint16_t *down;          /* fp16 down weight, row o at down + o*down_ld, F columns;
+                                      NULL loads a residual-only layer (ffnrm_residual only) */
     int64_t down_ld;               /* leading dimension of `down` in elements (>= F) */
     int32_t keep_fallback;         /* Q4_BYTES only: also keep the high codes for fallback tiles */
 } ffnrm_layer_weights;
@@ -217,6 +218,41 @@ int64_t ffnrm_launch_count(ffnrm_ctx *ctx);
 #define FFNRM_KERNEL_REDUCE 2
 int ffnrm_profile_enable(ffnrm_ctx *ctx, int enable);
 int ffnrm_profile_read(ffnrm_ctx *ctx, int kind, double *total_ms, int64_t *launches);
+
+/* ---- Host base producer (no GPU) ----------------------------------------------------
+ * The exact base sums of the split computed on the host's cores from the reference's
+ * radix table artifact (scripts/export_radix_table_artifact.py:17-80):
+ *   base[t, f] = sum_g s[t,g] * (alpha[f,g] * (multiplier * P_hi[t,f,g]) + beta[f,g] * zsum[t,g])
+ * with P_hi = sum_d 4^d sum_b table[b, state_d(b), f] - 128 * high_sum[f, g], exact in
+ * integers (multiplier = 2^r, 4 for the radix-4 tables). Replaces cpu_eval
+ * (src/exact_main_residual_cuda_runner.cu:144-187,
+ * src/exact_cpu_base_gpu_full_ffn_runner.cu:134-169) and the AVX2 fused evaluator
+ * (src/radix_cpu_kernels.h:143-217). Rows are produced in tiles of tile_rows by a
+ * pool of `threads` threads that claim tiles dynamically; the fp32 sum runs over the
+ * groups in order. */
+typedef struct ffnrm_base_producer ffnrm_base_producer;
+typedef struct {
+    int32_t rows;               /* F */
+    int32_t hidden;             /* D, a multiple of 32 */
+    int32_t block_size;         /* 2, 4 or 8 */
+    const uint8_t *table;       /* [hidden/block_size, 4^block_size, rows] */
+    const int16_t *high_sum;    /* [rows, hidden/32] */
+    const float *alpha, *beta;  /* [rows, hidden/32] */
+} ffnrm_radix_table;
+int ffnrm_base_producer_create(ffnrm_base_producer **out, int threads);
+int ffnrm_base_producer_destroy(ffnrm_base_producer *p);
+/* z [tokens, hidden] int8, s [tokens, hidden/32] f32, base [tokens, rows] f32 (host).
+ * tile_ready (optional) [tokens, ceil(rows/tile_rows)]: each entry is set to 1 (release
+ * store) when that tile's base values are written, so a consumer thread can stream
+ * finished tiles. deadline_ns > 0: tiles that finish later than that after the call
+ * started are flagged in late_tiles [ceil(rows/tile_rows)] (required then) for the
+ * exact GPU fallback path (ffnrm_ffn_forward's fallback_tiles), the deadline rule of
+ * src/phone_ffn_loopback.py:155-197; their values are still written. */
+int ffnrm_base_from_table(ffnrm_base_producer *p, const ffnrm_radix_table *table, const int8_t *z, const float *s,
+                          int tokens, int multiplier, float *base, int tile_rows, uint32_t *tile_ready,
+                          int64_t deadline_ns, uint8_t *late_tiles);
+/* The exact integer dots P_hi [rows, hidden/32] of one token (verification). */
+int ffnrm_table_dots(const ffnrm_radix_table *table, const int8_t *z, int32_t *dots);
 
 const char *ffnrm_last_error(void);
 const char *ffnrm_version(void);

@@ -25,6 +25,7 @@ fp16 down weights N(0,0.02).
 from __future__ import annotations
 
 import argparse
+import os
 import sys
 from pathlib import Path
 
@@ -79,12 +80,57 @@ def main() -> None:
         write_kats(quantize_groupwise_q8, pack_2bit_rows, pack_row_codes, compile_radix_table,
                    evaluate_radix_table, encode_signed_base4_states)
 
+    if args.only is None or "artifacts" in args.only:
+        make_artifacts()
+
     for name, (F, D, T, r, outliers, seed, tile_rows, flagged) in CASES.items():
         if args.only is not None and name not in args.only:
             continue
         make_case(name, F, D, T, r, outliers, seed, tile_rows, flagged, torch, compile_radix_table, direct_group_dots,
                   encode_signed_base4_states, evaluate_radix_table, pack_bitplanes, pack_row_codes, host_gpu_replay,
                   projection_from_group_dots, quantize_groupwise_q8)
+
+
+def make_artifacts():
+    """Artifact directories written by the reference's own exporters
+    (scripts/export_cuda_residual_artifact_v2.py:56-125 and
+    scripts/export_radix_table_artifact.py:17-80), run unmodified through their main()
+    with the GGUF loader replaced by the synthetic c1-shaped layer (96 rows, d_model
+    512; gate from seed 101, up from seed 108): ``artifact_residual_v2/`` and
+    ``artifact_table_b2/`` (block size 2)."""
+    import tempfile
+    import export_cuda_residual_artifact_v2 as exp_res
+    import export_radix_table_artifact as exp_tab
+    F, D, seed = 96, 512, 101
+    layers = {"gate": synth(F, D, 1, 0.0, seed), "up": synth(F, D, 1, 0.0, seed + 7)}
+
+    def fake_loader(model, layer, projection):
+        codes, alpha, beta, _, _ = layers[projection]
+        return codes.reshape(F, D // 32, 32), alpha, beta, int(codes.size // 2 + alpha.size * 2)
+
+    x = layers["gate"][3][0]
+    with tempfile.TemporaryDirectory() as tmp:
+        xin = Path(tmp) / "x.f32"
+        x.astype("<f4").tofile(xin)
+        exp_res.load_q4_projection = fake_loader
+        exp_tab.load_q4_projection = fake_loader
+        argv, cwd = sys.argv, os.getcwd()
+        os.chdir(tmp)  # the manifests record the input path: keep it relative
+        try:
+            sys.argv = ["export", "synthetic.gguf", "--layer", "23", "--input", xin.name,
+                        "--out", str(HERE / "artifact_residual_v2")]
+            exp_res.main()
+            sys.argv = ["export", "synthetic.gguf", xin.name, "--layer", "23", "--block-size", "2",
+                        "--out", str(HERE / "artifact_table_b2")]
+            exp_tab.main()
+        finally:
+            sys.argv = argv
+            os.chdir(cwd)
+    np.savez_compressed(HERE / "artifact_source.npz", F=F, D=D, x=x,
+                        **{f"{p}_{k}": v for p, (c, a, b, _, down) in layers.items()
+                           for k, v in (("codes", c), ("alpha", a), ("beta", b))},
+                        down=layers["gate"][4])
+    print("artifacts ok")
 
 
 def write_kats(quantize_groupwise_q8, pack_2bit_rows, pack_row_codes, compile_radix_table, evaluate_radix_table,
