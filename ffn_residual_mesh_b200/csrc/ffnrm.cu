@@ -70,6 +70,7 @@ struct LayerDev {
     // rows: the tensor-core A operand (built when batches larger than the GEMV's fit)
     DevBuf codes8;
     CUtensorMap codes8_map;  // box 128 codes x 128 rows, 128-byte swizzle
+    CUtensorMap codes8_map256;  // the same with boxes of the prefill B tile (kPfN rows)
     CUtensorMap down_map;    // TMA view of down [D][F16] fp16, box 64 x 128, 128-byte swizzle
 };
 
@@ -165,6 +166,7 @@ struct ffnrm_ctx {
     // (FFNRM_RESIDUAL_KERNEL=bytes|packed|mma)
     int res_kernel = 1;
     int prefill_tokens = 0;  // batches of at least this many tokens (no fallback tiles) take the prefill residual (0 = off)
+    int prefill_bytes = 1;   // the prefill residual reads the byte codes when the layer has them
     CUtensorMap h_map[4][2];             // h hi/lo views for token tiles 16, 32, 64, 128
     __half *h_hi = nullptr, *h_lo = nullptr;  // [Tm, F16] h = SiLU(g)*u as fp16 hi + lo
     // host-streamed mode staging, double-buffered per call
@@ -490,7 +492,7 @@ ffnrm::PfLayout prefill_layout(bool has_pair, bool has_plane, bool alpha_half, s
     L.off_alpha = L.off_plane + 2 * L.plane_bytes;
     L.src_bytes = L.off_alpha + 2 * L.alpha_bytes;
     const int a = kPfTokens * kPfKTile, w = kPfN * kPfKTile, al = 4 * kPfN * 4;
-    const int bars = (2 * (kPfMaxSA + kPfMaxS1 + kPfMaxSW + kPfMaxS4) + 2 * 2 + 1) * 8 + 16;
+    const int bars = (2 * (kPfMaxSA + kPfMaxS1 + kPfMaxSW + kPfMaxS4) + 2 * kPfBufs + 1) * 8 + 16;
     best.total = -1;
     int best_score = -1;
     for (int SW = 2; SW <= 3; ++SW)
@@ -517,20 +519,20 @@ ffnrm::PfLayout prefill_layout(bool has_pair, bool has_plane, bool alpha_half, s
     return best;
 }
 
-template <bool DOTS>
+template <bool DOTS, bool BYTES>
 int launch_residual_prefill_t(ffnrm_ctx *ctx, const LayerDev &L, ffnrm::ResidualParams &p, cudaStream_t st) {
     using namespace ffnrm;
     PfParams P{};
     P.rbits = ctx->cfg.residual_bits;
     P.alpha_half = L.scales_half ? 1 : 0;
     P.F64 = (p.F + 63) / 64;
-    const bool has_pair = P.rbits != 1;
-    if ((has_pair && !L.pair.ptr) || (P.rbits != 2 && !L.plane.ptr))
+    const bool has_pair = !BYTES && P.rbits != 1;
+    if ((has_pair && !L.pair.ptr) || (!BYTES && P.rbits != 2 && !L.plane.ptr))
         return fail(FFNRM_ERR_STATE, "layer lacks the code records the prefill residual reads");
-    P.L = prefill_layout(has_pair, P.rbits != 2, L.scales_half, 227 * 1024);
+    P.L = prefill_layout(has_pair, !BYTES && P.rbits != 2, L.scales_half, 227 * 1024);
     if (P.L.total < 0) return fail(FFNRM_ERR_ARG, "no shared-memory layout for the prefill residual");
     const size_t smem = size_t(P.L.total) + 1024;
-    auto kern = residual_prefill_kernel<DOTS>;
+    auto kern = residual_prefill_kernel<DOTS, BYTES>;
     // The warp-group register split (setmaxnreg) balances only at the launch register count
     // it was designed for; any other count would leave the drain's request unsatisfiable.
     cudaFuncAttributes fa{};
@@ -547,7 +549,7 @@ int launch_residual_prefill_t(ffnrm_ctx *ctx, const LayerDev &L, ffnrm::Residual
     P.p = p;
     dim3 grid(unsigned((p.T + kPfTokens - 1) / kPfTokens), unsigned((p.F + kPfRows - 1) / kPfRows));
     ProfScope prof(ctx, st, FFNRM_KERNEL_RESIDUAL);
-    FFNRM_CUDA(launch_dependent(kern, grid, dim3(kPfThreads), smem, st, true, 1, zm, P));
+    FFNRM_CUDA(launch_dependent(kern, grid, dim3(kPfThreads), smem, st, true, 1, zm, BYTES ? L.codes8_map256 : zm, P));
     ctx->launches++;
     return FFNRM_OK;
 }
@@ -572,7 +574,13 @@ int launch_residual_rb(ffnrm_ctx *ctx, const LayerDev &L, ffnrm::ResidualParams 
     }
     if (p.fallback_tiles == nullptr && ctx->prefill_tokens > 0 && p.T >= ctx->prefill_tokens &&
         (reinterpret_cast<uintptr_t>(p.s) & 15) == 0)  // the prefill drain reads s as float4
-        return p.dots ? launch_residual_prefill_t<true>(ctx, L, p, st) : launch_residual_prefill_t<false>(ctx, L, p, st);
+    {
+        if (L.codes8.ptr && ctx->prefill_bytes)
+            return p.dots ? launch_residual_prefill_t<true, true>(ctx, L, p, st)
+                          : launch_residual_prefill_t<false, true>(ctx, L, p, st);
+        return p.dots ? launch_residual_prefill_t<true, false>(ctx, L, p, st)
+                      : launch_residual_prefill_t<false, false>(ctx, L, p, st);
+    }
     if (ctx->res_kernel == 1 && p.fallback_tiles == nullptr && L.codes8.ptr &&
         ffnrm::ResTcCfg<32, false>::smem(p.G, 2) <= 227 * 1024) {
         if (p.T <= 16) return half ? launch_residual_tc_t<16, true>(ctx, L, p, st) : launch_residual_tc_t<16, false>(ctx, L, p, st);
@@ -780,6 +788,7 @@ int ffnrm_create(ffnrm_ctx **out, int device, const ffnrm_config *cfg) {
         ctx->res_kernel = std::strcmp(e, "packed") == 0 ? 0 : std::strcmp(e, "mma") == 0 ? 2 : 1;
     if (const char *e = std::getenv("FFNRM_GEMV_TOKENS")) ctx->gemv_tokens = std::max(1, std::atoi(e));
     if (const char *e = std::getenv("FFNRM_PREFILL_TOKENS")) ctx->prefill_tokens = std::max(0, std::atoi(e));
+    if (const char *e = std::getenv("FFNRM_PREFILL_BYTES")) ctx->prefill_bytes = std::atoi(e) != 0;
     cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
     const size_t TF = size_t(c.max_tokens) * c.d_ff, TD = size_t(c.max_tokens) * c.d_model;
     const size_t F16 = (size_t(c.d_ff) + 15) / 16 * 16;
@@ -928,7 +937,8 @@ int ffnrm_load_layer(ffnrm_ctx *ctx, int layer, const ffnrm_layer_weights *w) {
         (rc = dev_alloc(L.codes8, size_t(F64) * 128 * D)) == FFNRM_OK) {
         ffnrm::pack_codes8_kernel<<<pack_blocks(F64 * 128 * D / 16), 256>>>(lo[0], lo[1], F, D,
                                                                              static_cast<uint4 *>(L.codes8.ptr));
-        if (!make_u8_map(&L.codes8_map, L.codes8.ptr, uint64_t(D), uint64_t(F64 * 128), 128))
+        if (!make_u8_map(&L.codes8_map, L.codes8.ptr, uint64_t(D), uint64_t(F64 * 128), 128) ||
+            !make_u8_map(&L.codes8_map256, L.codes8.ptr, uint64_t(D), uint64_t(F64 * 128), ffnrm::kPfN))
             rc = fail(FFNRM_ERR_CUDA, "cuTensorMapEncodeTiled rejected the byte codes");
     }
     // fp16 down [D, ld] (F used columns) -> row-major [D][F16] with zero columns F..F16-1
@@ -1087,8 +1097,12 @@ int ffnrm_cast_f16(const float *src, uint16_t *dst, int64_t n, void *stream) {
 struct ffnrm_peer {
     int device = 0, world = 1, rank = 0;
     int64_t max_elems = 0;
-    void *region = nullptr;  // receive slots [2][world][max_elems] f32, then flags [world][chunks] u32
-    size_t recv_bytes = 0, region_bytes = 0;
+    // Region (CUDA IPC shared): one-shot receive slots [2][world][one_max] f32, one-shot
+    // flags [world][chunks] u32; then, when max_elems > one_max, the two-shot scatter and
+    // gather slots [2][world][stride] f32 each and their flags [world][chunks] u32 each.
+    void *region = nullptr;
+    int64_t one_max = 0, stride = 0;  // largest one-shot message; two-shot slice stride
+    size_t recv_bytes = 0, two_off = 0, region_bytes = 0;
     void *mapped[ffnrm::kPeerMaxRanks] = {};  // peers' regions opened here (own: region)
     uint32_t *counters = nullptr;              // epoch, done
     int *status = nullptr;
@@ -1109,8 +1123,19 @@ int ffnrm_peer_create(ffnrm_peer **out, int device, int world, int rank, int64_t
     pr->world = world;
     pr->rank = rank;
     pr->max_elems = max_elems;
-    pr->recv_bytes = size_t(2) * world * size_t(max_elems) * 4;
-    pr->region_bytes = pr->recv_bytes + size_t(world) * ffnrm::kPeerMaxChunks * 4;
+    // Messages above FFNRM_PEER_TWO_SHOT elements (default 2^20; 0 = never) take the
+    // two-shot reduce-scatter + all-gather, which needs far less receive space.
+    int64_t two_shot = int64_t(1) << 20;
+    if (const char *e = std::getenv("FFNRM_PEER_TWO_SHOT")) two_shot = std::atoll(e);
+    pr->one_max = two_shot > 0 ? std::min(max_elems, (two_shot + 3) / 4 * 4) : max_elems;
+    pr->recv_bytes = size_t(2) * world * size_t(pr->one_max) * 4;
+    const size_t flag_bytes = size_t(world) * ffnrm::kPeerMaxChunks * 4;
+    pr->two_off = pr->recv_bytes + flag_bytes;
+    pr->region_bytes = pr->two_off;
+    if (max_elems > pr->one_max) {
+        pr->stride = ((max_elems + world - 1) / world + 3) / 4 * 4;
+        pr->region_bytes += size_t(4) * world * size_t(pr->stride) * 4 + 2 * flag_bytes;
+    }
     cudaIpcMemHandle_t h;
     const bool ok = cudaMalloc(&pr->region, pr->region_bytes) == cudaSuccess &&
                     cudaMemset(pr->region, 0, pr->region_bytes) == cudaSuccess &&
@@ -1159,6 +1184,35 @@ int ffnrm_peer_allreduce(ffnrm_peer *pr, const float *partial, int64_t elems, ui
     if (!aligned(partial, 16) || (y32 && !aligned(y32, 16)) || (y16 && !aligned(y16, 8)))
         return fail(FFNRM_ERR_ARG, "partial and y32 must be 16-byte aligned, y16 8-byte aligned");
     DeviceGuard guard(pr->device);
+    if (elems > pr->one_max) {
+        ffnrm::PeerTwoShotParams q{};
+        const size_t slot_bytes = size_t(2) * pr->world * size_t(pr->stride) * 4;
+        const size_t flag_bytes = size_t(pr->world) * ffnrm::kPeerMaxChunks * 4;
+        for (int k = 0; k < pr->world; ++k) {
+            uint8_t *base = static_cast<uint8_t *>(pr->mapped[k]) + pr->two_off;
+            q.scatter[k] = reinterpret_cast<float *>(base);
+            q.gather[k] = reinterpret_cast<float *>(base + slot_bytes);
+            q.sflags[k] = reinterpret_cast<uint32_t *>(base + 2 * slot_bytes);
+            q.gflags[k] = reinterpret_cast<uint32_t *>(base + 2 * slot_bytes + flag_bytes);
+        }
+        q.partial = partial;
+        q.y16 = reinterpret_cast<__half *>(y16);
+        q.y32 = y32;
+        q.epoch = pr->counters;
+        q.done = pr->counters + 1;
+        q.status = pr->status;
+        q.elems = elems;
+        q.slice = ((elems + pr->world - 1) / pr->world + 3) / 4 * 4;
+        q.stride = pr->stride;
+        q.world = pr->world;
+        q.rank = pr->rank;
+        const int64_t per = (q.slice + ffnrm::kPeerMaxChunks - 1) / ffnrm::kPeerMaxChunks;
+        q.chunk = int(std::max<int64_t>(2048, (per + 3) / 4 * 4));
+        const int chunks = int((q.slice + q.chunk - 1) / q.chunk);
+        FFNRM_CUDA(launch_dependent(ffnrm::peer_two_shot_kernel, dim3(unsigned(chunks)), dim3(ffnrm::kPeerThreads), 0,
+                                    static_cast<cudaStream_t>(stream), true, 1, q));
+        return FFNRM_OK;
+    }
     ffnrm::PeerParams p{};
     for (int k = 0; k < pr->world; ++k) {
         p.recv[k] = static_cast<float *>(pr->mapped[k]);
@@ -1171,7 +1225,7 @@ int ffnrm_peer_allreduce(ffnrm_peer *pr, const float *partial, int64_t elems, ui
     p.done = pr->counters + 1;
     p.status = pr->status;
     p.elems = elems;
-    p.max_elems = pr->max_elems;
+    p.max_elems = pr->one_max;
     p.world = pr->world;
     p.rank = pr->rank;
     const int64_t per = (elems + ffnrm::kPeerMaxChunks - 1) / ffnrm::kPeerMaxChunks;

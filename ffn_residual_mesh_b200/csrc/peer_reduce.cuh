@@ -116,4 +116,137 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_kernel(const Peer
     }
 }
 
+
+// Two-shot variant for large partials (prefill: 2048 x 8192 fp32 = 64 MB per layer).
+// Pushing whole partials to every rank moves (world - 1) x the message per rank; here
+// rank r owns slice r of the output (elems / world, in chunks of `chunk`):
+//   1. CTA c pushes chunk c of every slice d of this rank's partial into rank d's
+//      scatter slot [epoch & 1][this rank] and raises scatter flag [this rank][c] there;
+//   2. it waits for chunk c of its own slice from every rank, sums them in rank order and
+//      pushes the sum (fp32) to every rank's gather slot [epoch & 1][this rank], raising
+//      gather flag [this rank][c] there;
+//   3. it waits for chunk c of every owner's summed slice and writes it to y (fp16 and/or
+//      fp32) at the slice's place.
+// Each rank sends (world - 1) / world of the message twice, about 2 x 64 MB x 7/8 at eight
+// ranks, instead of 7 x 64 MB. CTA c of one GPU waits only on CTA c of the others; the
+// grid fits on the GPU at once, so every CTA a wait depends on is running.
+struct PeerTwoShotParams {
+    float *scatter[kPeerMaxRanks];    // rank k's scatter slots [2][world][slice] (peer address)
+    float *gather[kPeerMaxRanks];     // rank k's gather slots [2][world][slice]
+    uint32_t *sflags[kPeerMaxRanks];  // rank k's scatter flags [world][kPeerMaxChunks]
+    uint32_t *gflags[kPeerMaxRanks];  // rank k's gather flags [world][kPeerMaxChunks]
+    const float *partial;
+    __half *y16;
+    float *y32;
+    uint32_t *epoch, *done;
+    int *status;
+    int64_t elems, slice;  // slice: elements per rank (a multiple of 4); the last rank's may be shorter
+    int64_t stride;        // elements between ranks' slots (the largest slice the region holds)
+    int chunk;             // elements per CTA within a slice, a multiple of 4
+    int world, rank;
+};
+
+__device__ __forceinline__ bool peer_wait_flag(volatile uint32_t *f, uint32_t ep, int *status) {
+    const long long t0 = clock64();
+    while (int32_t(*f - ep) < 0) {
+        if (clock64() - t0 > kPeerWaitCycles) {
+            atomicExch(status, 1);
+            return false;
+        }
+    }
+    return true;
+}
+
+__global__ void __launch_bounds__(kPeerThreads) peer_two_shot_kernel(const PeerTwoShotParams p) {
+    __shared__ uint32_t s_ep;
+    __shared__ int s_ok;
+    const int c = blockIdx.x;
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
+    if (threadIdx.x == 0) {
+        s_ep = *reinterpret_cast<volatile uint32_t *>(p.epoch) + 1u;
+        s_ok = 1;
+    }
+    __syncthreads();
+    const uint32_t ep = s_ep;
+    const int64_t slot = int64_t(ep & 1u) * p.world * p.stride;  // elements
+    // chunk c of slice d: [d*slice + c*chunk, min(...)) as float4 indices, relative to the slice
+    auto range = [&](int d, int64_t &b, int64_t &e) {
+        const int64_t s0 = int64_t(d) * p.slice, len = max(int64_t(0), min(p.elems, s0 + p.slice) - s0);
+        b = min(len, int64_t(c) * p.chunk) / 4;
+        e = min(len, int64_t(c + 1) * p.chunk) / 4;
+    };
+    // 1. scatter: chunk c of every slice d to rank d
+    const float4 *src = reinterpret_cast<const float4 *>(p.partial);
+    for (int d = 0; d < p.world; ++d) {
+        int64_t b, e;
+        range(d, b, e);
+        float4 *dst = reinterpret_cast<float4 *>(p.scatter[d] + slot + int64_t(p.rank) * p.stride);
+        const float4 *sd = src + int64_t(d) * p.slice / 4;
+        for (int64_t i = b + threadIdx.x; i < e; i += blockDim.x) dst[i] = __ldcg(sd + i);
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x < p.world)
+        *reinterpret_cast<volatile uint32_t *>(p.sflags[threadIdx.x] + p.rank * kPeerMaxChunks + c) = ep;
+    // 2. reduce chunk c of this rank's slice in rank order, push the sum to every rank
+    if (threadIdx.x < p.world && !peer_wait_flag(p.sflags[p.rank] + threadIdx.x * kPeerMaxChunks + c, ep, p.status))
+        s_ok = 0;
+    __syncthreads();
+    __threadfence();
+    {
+        int64_t b, e;
+        range(p.rank, b, e);
+        const float4 *in = reinterpret_cast<const float4 *>(p.scatter[p.rank] + slot);
+        const int64_t stride = p.stride / 4;
+        if (s_ok) {
+            for (int64_t i = b + threadIdx.x; i < e; i += blockDim.x) {
+                float4 a = __ldcg(in + i);
+                for (int k = 1; k < p.world; ++k) {
+                    const float4 v = __ldcg(in + int64_t(k) * stride + i);
+                    a.x += v.x;
+                    a.y += v.y;
+                    a.z += v.z;
+                    a.w += v.w;
+                }
+                for (int k = 0; k < p.world; ++k)
+                    reinterpret_cast<float4 *>(p.gather[k] + slot + int64_t(p.rank) * p.stride)[i] = a;
+            }
+        }
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x < p.world)
+        *reinterpret_cast<volatile uint32_t *>(p.gflags[threadIdx.x] + p.rank * kPeerMaxChunks + c) = ep;
+    // 3. gather: chunk c of every owner's sum into y
+    if (threadIdx.x < p.world && !peer_wait_flag(p.gflags[p.rank] + threadIdx.x * kPeerMaxChunks + c, ep, p.status))
+        s_ok = 0;
+    __syncthreads();
+    __threadfence();
+    if (s_ok) {
+        for (int d = 0; d < p.world; ++d) {
+            int64_t b, e;
+            range(d, b, e);
+            const float4 *g = reinterpret_cast<const float4 *>(p.gather[p.rank] + slot + int64_t(d) * p.stride);
+            const int64_t off = int64_t(d) * p.slice / 4;
+            for (int64_t i = b + threadIdx.x; i < e; i += blockDim.x) {
+                const float4 a = __ldcg(g + i);
+                if (p.y32) reinterpret_cast<float4 *>(p.y32)[off + i] = a;
+                if (p.y16) {
+                    __half2 *o = reinterpret_cast<__half2 *>(p.y16) + 2 * (off + i);
+                    o[0] = __floats2half2_rn(a.x, a.y);
+                    o[1] = __floats2half2_rn(a.z, a.w);
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(p.done, 1u) == gridDim.x - 1) {
+            *reinterpret_cast<volatile uint32_t *>(p.done) = 0u;
+            *reinterpret_cast<volatile uint32_t *>(p.epoch) = ep;
+        }
+    }
+}
+
 }  // namespace ffnrm

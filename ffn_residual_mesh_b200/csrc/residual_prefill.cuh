@@ -6,16 +6,19 @@
 // (row, token, group) dots per layer).
 //
 // Tile: tokens on the tensor-core M axis and rows on N. A CTA owns 128 tokens (TMEM
-// lanes) x 128 rows of both projections: N = 256 = the gate rows of row tile rt, then the
-// same rows of up. One tcgen05.mma kind::i8 (s8 activations x u8 codes -> s32, M = 128,
-// N = 256, K = 32) per 32-code group writes that group's exact dots P[token, row] into one
-// of two 256-column TMEM buffers; the scales are applied after, per group, in fp32.
+// lanes) x one 64-row record tile of both projections: N = 128 = its 64 gate rows, then
+// the same 64 up rows (the order of the layer's byte codes). One tcgen05.mma kind::i8
+// (s8 activations x u8 codes -> s32, M = 128, N = 128, K = 32) per 32-code group writes
+// that group's exact dots P[token, row] into one of four 128-column TMEM buffers, so the
+// MMAs run up to three groups ahead of the drain; the scales are applied after, per
+// group, in fp32.
 //
-// Why this shape: at prefill sizes the operand bytes that reach each SM, not HBM, are the
-// limit. Per 128-code K tile the CTA takes in 16 KB of activations (TMA) and 8 KB of
-// 2-bit code records (plus 2 KB of fp16 alpha) for 131 K dots, about 0.2 B per dot; a
-// 128-row x 32-token tile of byte codes needs 1.25 B. The code records are widened to one
-// byte per code in shared memory by two warps, one K tile ahead of the MMA.
+// Why this shape: at prefill sizes the operand bytes that reach each SM matter as much
+// as the arithmetic. Per 128-code K tile the CTA takes in 16 KB of activations (TMA)
+// and 4 KB of 2-bit code records (plus 1 KB of fp16 alpha), or 16 KB of byte codes,
+// for 65 K dots; a 128-row x 32-token tile of byte codes needs 1.25 B per dot. The code
+// records are widened to one byte per code in shared memory by two warps, one K tile
+// ahead of the MMA.
 //
 // Warp roles (384 threads, three warp groups):
 //   warp 0      producer: lane l < S1 owns code-record stage l (bulk copies of the two
@@ -23,12 +26,14 @@
 //               stages (2-D TMA, 128-byte swizzle).
 //   warp 1      TMEM allocation; lane 0 issues the MMAs.
 //   warps 2-3   widen the 2-bit (and plane) records into the K-major 128-byte-swizzled
-//               byte tile the MMA reads, and write the K tile's alphas as f32 [4][256].
-//   warps 4-19  drain, one token per thread (warp % 4 = TMEM lane quadrant), warp group
-//               h = 0..3 takes rows [32h, 32h+32) of both projections: 64 accumulators,
-//               per group acc += alpha[row] * (s[token] * float(P)) in packed fp32 pairs.
-// The first warp group gives registers to the four drain warp groups (setmaxnreg), so the
-// 64 accumulators per thread stay in registers next to a double-buffered TMEM chunk. The gate and up totals of a (token, row)
+//               byte tile the MMA reads, and write the K tile's alphas as f32 [4][128]
+//               (when the layer keeps byte codes, the producer brings the B tile by TMA
+//               instead and these warps only convert the alphas).
+//   warps 4-11  drain, one token per thread (warp % 4 = TMEM lane quadrant), warp group
+//               h = 0/1 takes rows [32h, 32h+32) of both projections: 64 accumulators,
+//               per group acc += alpha[row] * (s[token] * float(P)) in packed fp32 pairs,
+//               32-column TMEM loads double-buffered.
+// The first warp group gives registers to the two drain warp groups (setmaxnreg). The gate and up totals of a (token, row)
 // meet in the same thread: the epilogue merges them with the base sums and writes
 // h = SiLU(g)*u (fp16 hi + lo) with no exchange through shared memory.
 //
@@ -46,20 +51,22 @@
 namespace ffnrm {
 
 constexpr int kPfTokens = 128;             // tokens per CTA (M, TMEM lanes)
-constexpr int kPfRows = 128;               // rows per projection per CTA (N = 2 x 128)
+constexpr int kPfRows = 64;                // rows per projection per CTA (N = 2 x 64)
 constexpr int kPfN = 2 * kPfRows;          // MMA N
+constexpr int kPfSub = kPfRows / 64;       // 64-row record tiles per CTA
+constexpr int kPfBufs = 512 / kPfN;        // TMEM accumulator buffers (all 512 columns)
 constexpr int kPfKTile = 128;              // codes per K tile (4 groups, 2 record chunks)
-constexpr int kPfDrainWG = 4;              // drain warp groups
-constexpr int kPfThreads = 128 * (1 + kPfDrainWG);  // warp group 0 + the drain: 640
+constexpr int kPfDrainWG = 2;              // drain warp groups
+constexpr int kPfThreads = 128 * (1 + kPfDrainWG);  // warp group 0 + the drain: 384
 constexpr int kPfWiden = 64;               // widening threads (warps 2-3)
-constexpr int kPfDrain = 128 * kPfDrainWG;  // drain threads (warps 4..19)
-constexpr int kPfRpt = kPfRows / kPfDrainWG;  // rows of each projection per drain thread: 32
+constexpr int kPfDrain = 128 * kPfDrainWG;  // drain threads (warps 4..11)
+constexpr int kPfRpt = kPfRows / kPfDrainWG;  // rows of each projection per drain thread: 64
 constexpr int kPfRegsLow = 56;             // registers of warp group 0 after the split
-constexpr int kPfRegsHigh = 104;           // registers of the drain warp groups after it
-// Launched at R = 96 registers per thread (640 x 96 = 61440; five warps per scheduler),
-// the split gives (96 - 56) * 128 = 5120 registers and the drain takes (104 - 96) * 512 =
-// 4096 of them; per scheduler 56 + 4 * 104 = 472 <= 512 registers per lane.
-constexpr int kPfRegsLaunch = 96;
+constexpr int kPfRegsHigh = 224;           // registers of the drain warp groups after it
+// Launched at R = 168 registers per thread (384 x 168 = 64512; three warps per
+// scheduler), the split gives (168 - 56) * 128 = 14336 registers and the drain takes
+// (224 - 168) * 256 = 14336; per scheduler 56 + 2 * 224 = 504 <= 512 registers per lane.
+constexpr int kPfRegsLaunch = 168;
 constexpr int kPfMaxSA = 8, kPfMaxS1 = 8, kPfMaxSW = 4, kPfMaxS4 = 8;
 
 // Shared-memory layout (byte offsets; computed on the host by prefill_layout()).
@@ -79,13 +86,18 @@ struct PfParams {
     int F64;         // 64-row record tiles of the layer
 };
 
+// B tile / TMEM column order: the two 64-row record tiles of the CTA's 128 rows, each as
+// [64 gate rows | the same 64 up rows] (the layer's byte-code order): column
+// 128 u + 64 proj + m for row 64 u + m of projection proj.
 // Drain chunks: a thread's 2 * kPfRpt columns of a group (kPfRpt gate rows, the same up
-// rows) in kPfChunks chunks of kPfCh columns. TMEM column of chunk c for warp group h:
-// gate rows [kPfRpt h, kPfRpt (h+1)) are columns kPfRpt h.., up rows the same + 128.
-constexpr int kPfCh = 8;
+// rows) in kPfChunks chunks of kPfCh columns. Warp group h owns rows [kPfRpt h,
+// kPfRpt (h+1)): record tile u = kPfRpt h / 64, offset kPfRpt h % 64 inside it. A chunk is
+// the work between a TMEM load and its wait, so it must cover the load latency.
+constexpr int kPfCh = 32;
 constexpr int kPfChunks = 2 * kPfRpt / kPfCh;
+static_assert(kPfRpt == 32 || kPfRpt == 64, "drain warp groups own 32 or 64 rows");
 __device__ __forceinline__ constexpr int pf_col(int c, int h) {
-    return (c < kPfChunks / 2 ? 0 : kPfRows) + kPfRpt * h + kPfCh * (c % (kPfChunks / 2));
+    return 128 * (kPfRpt * h / 64) + (kPfRpt * h) % 64 + (c < kPfChunks / 2 ? 0 : 64) + kPfCh * (c % (kPfChunks / 2));
 }
 
 // SiLU(g)*u of two adjacent rows as fp16 hi + lo pairs (rows >= F are padding: zeros).
@@ -141,16 +153,18 @@ __device__ __forceinline__ void drain_prefill(const ResidualParams &p, const PfP
             if (ok) sm100::tmem_wait_ld();  // chunk st has landed
             if (c == kPfChunks - 1) {       // last chunk of the group: release its buffer
                 sm100::tc_fence_before();
-                sm100::mbar_arrive(acc_empty + (gi & 1));
+                sm100::mbar_arrive(acc_empty + gi % kPfBufs);
             }
             const int gn = c == kPfChunks - 1 ? gi + 1 : gi, cn = (c + 1) % kPfChunks;
             if (gn < 4 * nkt && ok) {
                 if (cn == 0) {
                     ok = __all_sync(0xffffffffu,
-                                    sm100::mbar_wait(acc_full + (gn & 1), (gn >> 1) & 1, p.err, sm100::kErrWaitFull));
+                                    sm100::mbar_wait(acc_full + gn % kPfBufs, (gn / kPfBufs) & 1, p.err,
+                                                     sm100::kErrWaitFull));
                     sm100::tc_fence_after();
                 }
-                if (ok) sm100::tmem_ld<kPfCh>(lane_base + uint32_t((gn & 1) * kPfN + pf_col(cn, h)), rb[(st + 1) & 1]);
+                if (ok)
+                    sm100::tmem_ld<kPfCh>(lane_base + uint32_t((gn % kPfBufs) * kPfN + pf_col(cn, h)), rb[(st + 1) & 1]);
             }
             if (ok) {
                 const uint32_t *r = rb[st & 1];
@@ -221,24 +235,27 @@ __device__ __forceinline__ void drain_prefill(const ResidualParams &p, const PfP
     }
 }
 
-template <bool DOTS>
+// BYTES: the layer's byte codes arrive in the B tile by TMA (tm_w, kPfN-row box) and the
+// widening warps only convert the alphas; otherwise they widen the 2-bit records.
+template <bool DOTS, bool BYTES>
 __global__ void __launch_bounds__(kPfThreads, 1)
-    residual_prefill_kernel(const __grid_constant__ CUtensorMap tm_z, const PfParams P) {
+    residual_prefill_kernel(const __grid_constant__ CUtensorMap tm_z, const __grid_constant__ CUtensorMap tm_w,
+                            const PfParams P) {
     const ResidualParams &p = P.p;
     const PfLayout &Ly = P.L;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *a_ring = smem;                 // [SA][128 tokens][128 B] activations
-    uint8_t *w_ring = smem + Ly.w_off;      // [SW][256 rows][128 B] widened codes
+    uint8_t *w_ring = smem + Ly.w_off;      // [SW][kPfN rows][128 B] widened codes
     uint8_t *src_ring = smem + Ly.src_off;  // [S1] records + alphas of the two 64-row tiles
-    float *al_ring = reinterpret_cast<float *>(smem + Ly.al_off);  // [S4][4 groups][256] f32 alphas
+    float *al_ring = reinterpret_cast<float *>(smem + Ly.al_off);  // [S4][4 groups][kPfN] f32 alphas
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Ly.bar_off);
     uint64_t *a_full = bars, *a_empty = a_full + kPfMaxSA;
     uint64_t *src_full = a_empty + kPfMaxSA, *src_empty = src_full + kPfMaxS1;
     uint64_t *w_full = src_empty + kPfMaxS1, *w_empty = w_full + kPfMaxSW;
     uint64_t *al_full = w_empty + kPfMaxSW, *al_empty = al_full + kPfMaxS4;
-    uint64_t *acc_full = al_empty + kPfMaxS4, *acc_empty = acc_full + 2;
-    uint64_t *done = acc_empty + 2;
+    uint64_t *acc_full = al_empty + kPfMaxS4, *acc_empty = acc_full + kPfBufs;
+    uint64_t *done = acc_empty + kPfBufs;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -246,7 +263,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const int rt = blockIdx.y, t0 = blockIdx.x * kPfTokens;
     const int nkt = p.D / kPfKTile;
     const int SA = Ly.SA, S1 = Ly.S1, SW = Ly.SW, S4 = Ly.S4;
-    const bool sub1 = 2 * rt + 1 < P.F64;  // the second 64-row tile exists
+    const bool sub1 = kPfSub == 2 && 2 * rt + 1 < P.F64;  // a second 64-row tile exists
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < SA; ++s) {
@@ -258,14 +275,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             sm100::mbar_init(src_empty + s, kPfWiden);
         }
         for (int s = 0; s < SW; ++s) {
-            sm100::mbar_init(w_full + s, kPfWiden);
+            sm100::mbar_init(w_full + s, BYTES ? 1 : kPfWiden);
             sm100::mbar_init(w_empty + s, 1);
         }
         for (int s = 0; s < S4; ++s) {
             sm100::mbar_init(al_full + s, kPfWiden);
             sm100::mbar_init(al_empty + s, kPfDrain);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < kPfBufs; ++b) {
             sm100::mbar_init(acc_full + b, 1);
             sm100::mbar_init(acc_empty + b, kPfDrain);
         }
@@ -289,9 +306,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         if (warp == 0) {
             // Producer. A lane reuses only its own stage, in order, so each parity test is at
             // most one phase ahead of its barrier; the warp polls with non-blocking tests.
-            const int role = lane < S1 ? 0 : lane < S1 + SA ? 1 : -1;
-            const int st = role == 0 ? lane : role == 1 ? lane - S1 : 0;
-            const int depth = role == 0 ? S1 : SA;
+            // roles: 0 = record/alpha stages, 1 = activation stages, 2 = byte-code B tiles
+            const int role = lane < S1 ? 0 : lane < S1 + SA ? 1 : (BYTES && lane < S1 + SA + SW) ? 2 : -1;
+            const int st = role == 0 ? lane : role == 1 ? lane - S1 : role == 2 ? lane - S1 - SA : 0;
+            const int depth = role == 0 ? S1 : role == 1 ? SA : SW;
             const uint32_t src_tx = uint32_t(Ly.pair_bytes + Ly.plane_bytes + Ly.alpha_bytes) * (sub1 ? 2u : 1u);
             const int ab = P.alpha_half ? 4 : 8;  // alpha bytes per record
             auto issue = [&](int kt) {
@@ -299,7 +317,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     uint8_t *src = src_ring + st * Ly.src_bytes;
                     sm100::mbar_arrive_expect_tx(src_full + st, src_tx);
                     for (int u = 0; u < (sub1 ? 2 : 1); ++u) {
-                        const int64_t rec = (int64_t(2 * rt + u) * C + 2 * kt) * 128;  // chunks 2kt, 2kt+1
+                        const int64_t rec = (int64_t(kPfSub * rt + u) * C + 2 * kt) * 128;  // chunks 2kt, 2kt+1
                         if (Ly.pair_bytes)
                             sm100::bulk_load(src + Ly.off_pair + u * Ly.pair_bytes, p.proj[0].pair + rec, Ly.pair_bytes,
                                              src_full + st);
@@ -310,20 +328,24 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                                          static_cast<const uint8_t *>(p.proj[0].alpha) + rec * ab, Ly.alpha_bytes,
                                          src_full + st);
                     }
-                } else {
+                } else if (role == 1) {
                     sm100::mbar_arrive_expect_tx(a_full + st, kPfTokens * kPfKTile);
                     sm100::tma_load_2d(a_ring + st * (kPfTokens * kPfKTile), &tm_z, kt * kPfKTile, t0, a_full + st);
+                } else {
+                    // rows [kPfN rt, kPfN (rt + 1)) of the byte codes: gate|up of the record tile(s)
+                    sm100::mbar_arrive_expect_tx(w_full + st, kPfN * kPfKTile);
+                    sm100::tma_load_2d(w_ring + st * (kPfN * kPfKTile), &tm_w, kt * kPfKTile, kPfN * rt, w_full + st);
                 }
             };
             int kt = role >= 0 ? st : nkt;
             // Weights (fresh stages) go out before the dependency wait; activations, which come
             // from the preceding kernel of the stream, only after it.
-            if (role == 0) {
+            if (role == 0 || role == 2) {
                 if (kt < nkt) issue(kt);
                 kt += depth;
             }
             sm100::grid_dependency_wait();
-            uint64_t *empty = role == 0 ? src_empty : a_empty;
+            uint64_t *empty = role == 0 ? src_empty : role == 1 ? a_empty : w_empty;
             long long last = clock64();
             while (__any_sync(0xffffffffu, kt < nkt)) {
                 const bool ready = kt < nkt && sm100::mbar_test_wait(empty + st, ((kt / depth) & 1) ^ 1);
@@ -344,7 +366,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             // use of its stage (earlier uses completed before the stage was refilled).
             if (role >= 0 && st < nkt) {
                 const int last_kt = st + (nkt - 1 - st) / depth * depth;
-                sm100::mbar_wait((role == 0 ? src_full : a_full) + st, (last_kt / depth) & 1, p.err, sm100::kErrWaitFull);
+                sm100::mbar_wait((role == 0 ? src_full : role == 1 ? a_full : w_full) + st, (last_kt / depth) & 1, p.err,
+                                 sm100::kErrWaitFull);
             }
         } else if (warp == 1) {
             if (lane == 0) {  // MMA issuer
@@ -360,8 +383,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     const uint32_t w = sm100::smem_u32(w_ring + sw * (kPfN * kPfKTile));
     #pragma unroll
                     for (int j = 0; j < 4; ++j) {
-                        const int gi = 4 * kt + j, b = gi & 1;
-                        if (!(ok = sm100::mbar_wait(acc_empty + b, ((gi >> 1) & 1) ^ 1, p.err, sm100::kErrWaitEmpty))) break;
+                        const int gi = 4 * kt + j, b = gi % kPfBufs;
+                        if (!(ok = sm100::mbar_wait(acc_empty + b, ((gi / kPfBufs) & 1) ^ 1, p.err, sm100::kErrWaitEmpty)))
+                            break;
                         sm100::tc_fence_after();
                         sm100::umma_i8(tmem + uint32_t(b * kPfN), sm100::umma_desc_sw128(a + 32 * j),
                                        sm100::umma_desc_sw128(w + 32 * j), idesc, 0);
@@ -385,17 +409,18 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 if (ok)
                     ok = __all_sync(0xffffffffu,
                                     sm100::mbar_wait(src_full + s1, (kt / S1) & 1, p.err, sm100::kErrWaitFull) &&
-                                        sm100::mbar_wait(w_empty + sw, ((kt / SW) & 1) ^ 1, p.err, sm100::kErrWaitEmpty) &&
+                                        (BYTES ||
+                                         sm100::mbar_wait(w_empty + sw, ((kt / SW) & 1) ^ 1, p.err, sm100::kErrWaitEmpty)) &&
                                         sm100::mbar_wait(al_empty + s4, ((kt / S4) & 1) ^ 1, p.err, sm100::kErrWaitEmpty));
                 if (ok) {
                     const uint8_t *src = src_ring + s1 * Ly.src_bytes;
                     uint8_t *W = w_ring + sw * (kPfN * kPfKTile);
                     float *AL = al_ring + s4 * (4 * kPfN);
     #pragma unroll 2
-                    for (int i = 0; i < 8; ++i) {
+                    for (int i = 0; i < 4 * kPfSub; ++i) {
                         const int rec = wt + 64 * i;
                         const int u = rec >> 8, cc = (rec >> 7) & 1, m = rec & 127;
-                        const int n = (m & 64 ? kPfRows : 0) + 64 * u + (m & 63);
+                        const int n = 128 * u + m;
                         const int ridx = cc * 128 + m;
                         uint4 w = make_uint4(0, 0, 0, 0);
                         uint2 pw = make_uint2(0, 0);
@@ -409,6 +434,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                             else
                                 load_scale2_shared<false>(al, ridx, a0, a1);
                         }
+                        AL[(2 * cc) * kPfN + n] = a0;
+                        AL[(2 * cc + 1) * kPfN + n] = a1;
+                        if (BYTES) continue;  // the codes arrived by TMA
                         const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
                         uint8_t *row = W + n * kPfKTile;
     #pragma unroll
@@ -420,12 +448,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                             const int unit = 4 * cc + jj;
                             *reinterpret_cast<uint4 *>(row + ((unit ^ (n & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
                         }
-                        AL[(2 * cc) * kPfN + n] = a0;
-                        AL[(2 * cc + 1) * kPfN + n] = a1;
                     }
-                    sm100::fence_proxy_async_smem();  // generic-proxy stores -> tensor-core operand reads
+                    if (!BYTES) sm100::fence_proxy_async_smem();  // generic-proxy stores -> tensor-core operand reads
                 }
-                sm100::mbar_arrive(w_full + sw);
+                if (!BYTES) sm100::mbar_arrive(w_full + sw);
                 sm100::mbar_arrive(al_full + s4);
                 sm100::mbar_arrive(src_empty + s1);
             }

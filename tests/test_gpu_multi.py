@@ -27,7 +27,12 @@ def _rank(rank, world, port, mode, out):
 
     import torch
     import torch.distributed as dist
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), FFNRM_PEER_REDUCE=mode, NCCL_NVLS_ENABLE="0")
+    # mode: "1" peer kernel (one-shot below 2^20 elements), "2" peer kernel with the two-shot
+    # reduce-scatter + all-gather from 1024 elements, "0" NCCL allreduce + cast
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), FFNRM_PEER_REDUCE="0" if mode == "0" else "1",
+                      NCCL_NVLS_ENABLE="0")
+    if mode == "2":
+        os.environ["FFNRM_PEER_TWO_SHOT"] = "1024"
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
@@ -72,7 +77,7 @@ def _rank(rank, world, port, mode, out):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["1", "0"], ids=["peer", "nccl"])
+@pytest.mark.parametrize("mode", ["1", "2", "0"], ids=["peer", "peer_two_shot", "nccl"])
 def test_two_gpu_sharded_stack(mode):
     import torch
     if torch.cuda.device_count() < 2:
@@ -81,7 +86,7 @@ def test_two_gpu_sharded_stack(mode):
     from oracle import ffnrm_oracle as O
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29600 + os.getpid() % 500 + (7 if mode == "0" else 0)
+    port = 29600 + os.getpid() % 500 + 7 * int(mode)
     procs = [ctx.Process(target=_rank, args=(k, 2, port, mode, q)) for k in range(2)]
     for p in procs:
         p.start()
@@ -106,3 +111,60 @@ def test_two_gpu_sharded_stack(mode):
         y = y0.astype(np.float64)
         assert np.abs(y - ref).max() < Y_MAX_ABS
         assert np.linalg.norm(y - ref) / np.linalg.norm(ref) < Y_REL_L2
+
+
+def _rank_skip(rank, world, port, out, released):
+    """Rank 1 leaves between steps: it skips the second reduction. Rank 0's kernel gives up
+    its bounded wait (about a second) and the host sees FFNRM_ERR_TIMEOUT."""
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    from ffn_residual_mesh_b200.shard import PeerReduce
+    n = 4096
+    peer = PeerReduce(world, rank, rank, n)
+    try:
+        x = torch.full((n,), float(rank + 1), device="cuda")
+        y = torch.empty(n, dtype=torch.float16, device="cuda")
+        peer.allreduce(x, y16=y)
+        peer.check()
+        first = float(y[0])
+        if rank == 0:
+            peer.allreduce(x, y16=y)  # rank 1 never makes this call
+            try:
+                peer.check()
+                result = "no timeout"
+            except TimeoutError as e:
+                result = "timeout: " + str(e)
+            released.set()
+        else:
+            released.wait(timeout=120)
+            result = "skipped"
+        out.put((rank, first, result))
+    finally:
+        torch.cuda.synchronize()
+        peer.close()
+        dist.destroy_process_group()
+
+
+def test_peer_wait_times_out_when_a_rank_stops():
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    q, released = ctx.Queue(), ctx.Event()
+    port = 29900 + os.getpid() % 500
+    procs = [ctx.Process(target=_rank_skip, args=(k, 2, port, q, released)) for k in range(2)]
+    for p in procs:
+        p.start()
+    got = dict((r, (f, res)) for r, f, res in (q.get(timeout=300) for _ in range(2)))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert got[0][0] == got[1][0] == 3.0  # the first reduction completed on both ranks
+    assert got[0][1].startswith("timeout"), got[0][1]
+    assert got[1][1] == "skipped"
