@@ -70,7 +70,6 @@ struct LayerDev {
     // rows: the tensor-core A operand (built when batches larger than the GEMV's fit)
     DevBuf codes8;
     CUtensorMap codes8_map;  // box 128 codes x 128 rows, 128-byte swizzle
-    CUtensorMap codes8_map256;  // the same with boxes of the prefill B tile (kPfN rows)
     CUtensorMap down_map;    // TMA view of down [D][F16] fp16, box 64 x 128, 128-byte swizzle
 };
 
@@ -166,7 +165,6 @@ struct ffnrm_ctx {
     // (FFNRM_RESIDUAL_KERNEL=bytes|packed|mma)
     int res_kernel = 1;
     int prefill_tokens = 0;  // batches of at least this many tokens (no fallback tiles) take the prefill residual (0 = off)
-    int prefill_bytes = 1;   // the prefill residual reads the byte codes when the layer has them
     CUtensorMap h_map[4][2];             // h hi/lo views for token tiles 16, 32, 64, 128
     __half *h_hi = nullptr, *h_lo = nullptr;  // [Tm, F16] h = SiLU(g)*u as fp16 hi + lo
     // host-streamed mode staging, double-buffered per call
@@ -175,6 +173,7 @@ struct ffnrm_ctx {
     float *base_dev[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};  // [slot][proj] [Tm, F]
     uint8_t *tiles_dev[2] = {nullptr, nullptr};
     uint16_t *y16_dev = nullptr;
+    void *z16 = nullptr;  // [Tm, D] fp16 activations for the prefill residual
     cudaStream_t copy_stream = nullptr;
     cudaEvent_t base_ready[2] = {nullptr, nullptr}, slot_free[2] = {nullptr, nullptr};
     int slot = 0;
@@ -478,24 +477,24 @@ int launch_residual_umma_t(ffnrm_ctx *ctx, const LayerDev &L, ffnrm::ResidualPar
 }
 
 // Shared-memory layout of the prefill residual: ring depths chosen to fit one CTA per SM.
-// Activations (SA) and code records (S1) cover the L2/HBM latency (~4 K tiles each),
-// widened codes (SW) one K tile of widening ahead of the MMA, f32 alphas (S4) the lag
-// of the drain behind the widening (the MMA runs up to two groups ahead of the drain).
+// Activations (SA) and code records (S1) cover the L2/HBM latency (several K tiles each),
+// widened codes (SW) the widening ahead of the MMA, f32 alphas (S4) the lag of the drain
+// behind the widening (the MMAs run up to kPfBufs groups ahead of the drain).
 ffnrm::PfLayout prefill_layout(bool has_pair, bool has_plane, bool alpha_half, size_t budget) {
     using namespace ffnrm;
     PfLayout L{}, best{};
-    L.pair_bytes = has_pair ? 4096 : 0;
-    L.plane_bytes = has_plane ? 2048 : 0;
-    L.alpha_bytes = alpha_half ? 1024 : 2048;
+    L.pair_bytes = has_pair ? 128 * 16 : 0;  // one chunk of 128 records
+    L.plane_bytes = has_plane ? 128 * 8 : 0;
+    L.alpha_bytes = 128 * (alpha_half ? 4 : 8);
     L.off_pair = 0;
-    L.off_plane = 2 * L.pair_bytes;
-    L.off_alpha = L.off_plane + 2 * L.plane_bytes;
-    L.src_bytes = L.off_alpha + 2 * L.alpha_bytes;
-    const int a = kPfTokens * kPfKTile, w = kPfN * kPfKTile, al = 4 * kPfN * 4;
+    L.off_plane = L.pair_bytes;
+    L.off_alpha = L.off_plane + L.plane_bytes;
+    L.src_bytes = L.off_alpha + L.alpha_bytes;
+    const int a = kPfTokens * kPfRowBytes, w = kPfN * kPfRowBytes, al = 2 * kPfN * 4;
     const int bars = (2 * (kPfMaxSA + kPfMaxS1 + kPfMaxSW + kPfMaxS4) + 2 * kPfBufs + 1) * 8 + 16;
     best.total = -1;
     int best_score = -1;
-    for (int SW = 2; SW <= 3; ++SW)
+    for (int SW = 2; SW <= kPfMaxSW; ++SW)
         for (int SA = 2; SA <= kPfMaxSA; ++SA)
             for (int S1 = 2; S1 <= kPfMaxS1; ++S1)
                 for (int S4 = 2; S4 <= kPfMaxS4; ++S4) {
@@ -509,8 +508,8 @@ ffnrm::PfLayout prefill_layout(bool has_pair, bool has_plane, bool alpha_half, s
                     L.bar_off = (L.al_off + S4 * al + 7) / 8 * 8;
                     L.total = L.bar_off + bars;
                     if (size_t(L.total) + 1024 > budget) continue;
-                    const int score = 4 * std::min(SA, 4) + 4 * std::min(S1, 4) + 3 * std::min(S4, 4) + 2 * SW +
-                                      std::min(SA, 6) + std::min(S1, 6) + std::min(S4, 6) / 2;
+                    const int score = 4 * std::min(SA, 6) + 4 * std::min(S1, 6) + 3 * std::min(S4, 6) + 3 * std::min(SW, 3) +
+                                      SA + S1 + S4 / 2;
                     if (score > best_score || (score == best_score && L.total < best.total)) {
                         best_score = score;
                         best = L;
@@ -519,37 +518,36 @@ ffnrm::PfLayout prefill_layout(bool has_pair, bool has_plane, bool alpha_half, s
     return best;
 }
 
-template <bool DOTS, bool BYTES>
+template <bool DOTS>
 int launch_residual_prefill_t(ffnrm_ctx *ctx, const LayerDev &L, ffnrm::ResidualParams &p, cudaStream_t st) {
     using namespace ffnrm;
     PfParams P{};
     P.rbits = ctx->cfg.residual_bits;
     P.alpha_half = L.scales_half ? 1 : 0;
-    P.F64 = (p.F + 63) / 64;
-    const bool has_pair = !BYTES && P.rbits != 1;
-    if ((has_pair && !L.pair.ptr) || (!BYTES && P.rbits != 2 && !L.plane.ptr))
+    const bool has_pair = P.rbits != 1;
+    if ((has_pair && !L.pair.ptr) || (P.rbits != 2 && !L.plane.ptr))
         return fail(FFNRM_ERR_STATE, "layer lacks the code records the prefill residual reads");
-    P.L = prefill_layout(has_pair, !BYTES && P.rbits != 2, L.scales_half, 227 * 1024);
+    if (!ctx->z16) return fail(FFNRM_ERR_STATE, "no fp16 activation workspace");
+    P.L = prefill_layout(has_pair, P.rbits != 2, L.scales_half, 227 * 1024);
     if (P.L.total < 0) return fail(FFNRM_ERR_ARG, "no shared-memory layout for the prefill residual");
     const size_t smem = size_t(P.L.total) + 1024;
-    auto kern = residual_prefill_kernel<DOTS, BYTES>;
-    // The warp-group register split (setmaxnreg) balances only at the launch register count
-    // it was designed for; any other count would leave the drain's request unsatisfiable.
-    cudaFuncAttributes fa{};
-    FFNRM_CUDA(cudaFuncGetAttributes(&fa, kern));
-    if (fa.numRegs != kPfRegsLaunch)
-        return fail(FFNRM_ERR_STATE, "prefill residual built with %d registers per thread, needs %d", fa.numRegs,
-                    kPfRegsLaunch);
+    auto kern = residual_prefill_kernel<DOTS>;
     CUtensorMap zm;
-    if (!make_z_map(&zm, p.z, uint64_t(p.D), uint64_t(p.T), kPfTokens))
-        return fail(FFNRM_ERR_CUDA, "cuTensorMapEncodeTiled rejected the activations");
+    if (!make_fp16_map(&zm, ctx->z16, uint64_t(p.D), uint64_t(p.T), uint64_t(p.D), kPfTokens))
+        return fail(FFNRM_ERR_CUDA, "cuTensorMapEncodeTiled rejected the fp16 activations");
     FFNRM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+    // z -> fp16 (exact) into the workspace, then the residual as its dependent
+    const int64_t n = int64_t(p.T) * p.D;
+    const int cblocks = int(std::min<int64_t>((n / 16 + 255) / 256, int64_t(ctx->num_sms) * 8));
+    FFNRM_CUDA(launch_dependent(z_to_f16_kernel, dim3(unsigned(cblocks)), dim3(256), 0, st, false, 1, p.z,
+                                static_cast<__half *>(ctx->z16), n));
+    ctx->launches++;
     p.row_blocks = (p.F + 31) / 32;
     p.err = ctx->err;
     P.p = p;
     dim3 grid(unsigned((p.T + kPfTokens - 1) / kPfTokens), unsigned((p.F + kPfRows - 1) / kPfRows));
     ProfScope prof(ctx, st, FFNRM_KERNEL_RESIDUAL);
-    FFNRM_CUDA(launch_dependent(kern, grid, dim3(kPfThreads), smem, st, true, 1, zm, BYTES ? L.codes8_map256 : zm, P));
+    FFNRM_CUDA(launch_dependent(kern, grid, dim3(kPfThreads), smem, st, true, 1, zm, P));
     ctx->launches++;
     return FFNRM_OK;
 }
@@ -573,14 +571,8 @@ int launch_residual_rb(ffnrm_ctx *ctx, const LayerDev &L, ffnrm::ResidualParams 
         return launch_residual_mma_nt<RB, 4>(ctx, p, half, st);  // 32-token tiles (64 would spill)
     }
     if (p.fallback_tiles == nullptr && ctx->prefill_tokens > 0 && p.T >= ctx->prefill_tokens &&
-        (reinterpret_cast<uintptr_t>(p.s) & 15) == 0)  // the prefill drain reads s as float4
-    {
-        if (L.codes8.ptr && ctx->prefill_bytes)
-            return p.dots ? launch_residual_prefill_t<true, true>(ctx, L, p, st)
-                          : launch_residual_prefill_t<false, true>(ctx, L, p, st);
-        return p.dots ? launch_residual_prefill_t<true, false>(ctx, L, p, st)
-                      : launch_residual_prefill_t<false, false>(ctx, L, p, st);
-    }
+        (reinterpret_cast<uintptr_t>(p.s) & 7) == 0 && (reinterpret_cast<uintptr_t>(p.z) & 15) == 0)
+        return p.dots ? launch_residual_prefill_t<true>(ctx, L, p, st) : launch_residual_prefill_t<false>(ctx, L, p, st);
     if (ctx->res_kernel == 1 && p.fallback_tiles == nullptr && L.codes8.ptr &&
         ffnrm::ResTcCfg<32, false>::smem(p.G, 2) <= 227 * 1024) {
         if (p.T <= 16) return half ? launch_residual_tc_t<16, true>(ctx, L, p, st) : launch_residual_tc_t<16, false>(ctx, L, p, st);
@@ -788,7 +780,6 @@ int ffnrm_create(ffnrm_ctx **out, int device, const ffnrm_config *cfg) {
         ctx->res_kernel = std::strcmp(e, "packed") == 0 ? 0 : std::strcmp(e, "mma") == 0 ? 2 : 1;
     if (const char *e = std::getenv("FFNRM_GEMV_TOKENS")) ctx->gemv_tokens = std::max(1, std::atoi(e));
     if (const char *e = std::getenv("FFNRM_PREFILL_TOKENS")) ctx->prefill_tokens = std::max(0, std::atoi(e));
-    if (const char *e = std::getenv("FFNRM_PREFILL_BYTES")) ctx->prefill_bytes = std::atoi(e) != 0;
     cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
     const size_t TF = size_t(c.max_tokens) * c.d_ff, TD = size_t(c.max_tokens) * c.d_model;
     const size_t F16 = (size_t(c.d_ff) + 15) / 16 * 16;
@@ -796,7 +787,7 @@ int ffnrm_create(ffnrm_ctx **out, int device, const ffnrm_config *cfg) {
     bool ok = cudaMalloc(&ctx->err, sizeof(int)) == cudaSuccess && cudaMemset(ctx->err, 0, sizeof(int)) == cudaSuccess &&
               cudaMalloc(&ctx->h_hi, size_t(c.max_tokens) * F16 * 2) == cudaSuccess &&
               cudaMalloc(&ctx->h_lo, size_t(c.max_tokens) * F16 * 2) == cudaSuccess &&
-              cudaMalloc(&ctx->y16_dev, TD * 2) == cudaSuccess;
+              cudaMalloc(&ctx->y16_dev, TD * 2) == cudaSuccess && cudaMalloc(&ctx->z16, TD * 2) == cudaSuccess;
     for (int sl = 0; sl < 2 && ok; ++sl) {
         ok = cudaMalloc(&ctx->base_dev[sl][0], TF * 4) == cudaSuccess && cudaMalloc(&ctx->base_dev[sl][1], TF * 4) == cudaSuccess &&
              cudaMalloc(&ctx->tiles_dev[sl], size_t(ntiles)) == cudaSuccess &&
@@ -833,6 +824,7 @@ int ffnrm_destroy(ffnrm_ctx *ctx) {
     cudaFree(ctx->h_hi);
     cudaFree(ctx->h_lo);
     cudaFree(ctx->y16_dev);
+    cudaFree(ctx->z16);
     for (int sl = 0; sl < 2; ++sl) {
         cudaFree(ctx->base_dev[sl][0]);
         cudaFree(ctx->base_dev[sl][1]);
@@ -937,8 +929,7 @@ int ffnrm_load_layer(ffnrm_ctx *ctx, int layer, const ffnrm_layer_weights *w) {
         (rc = dev_alloc(L.codes8, size_t(F64) * 128 * D)) == FFNRM_OK) {
         ffnrm::pack_codes8_kernel<<<pack_blocks(F64 * 128 * D / 16), 256>>>(lo[0], lo[1], F, D,
                                                                              static_cast<uint4 *>(L.codes8.ptr));
-        if (!make_u8_map(&L.codes8_map, L.codes8.ptr, uint64_t(D), uint64_t(F64 * 128), 128) ||
-            !make_u8_map(&L.codes8_map256, L.codes8.ptr, uint64_t(D), uint64_t(F64 * 128), ffnrm::kPfN))
+        if (!make_u8_map(&L.codes8_map, L.codes8.ptr, uint64_t(D), uint64_t(F64 * 128), 128))
             rc = fail(FFNRM_ERR_CUDA, "cuTensorMapEncodeTiled rejected the byte codes");
     }
     // fp16 down [D, ld] (F used columns) -> row-major [D][F16] with zero columns F..F16-1

@@ -1,10 +1,10 @@
-"""GPU parity of the prefill residual (tokens on the tensor-core M axis, 128 rows of both
-projections on N, 2-bit records widened in shared memory), through the C ABI.
+"""GPU parity of the prefill residual (tokens on the tensor-core M axis, 64 rows of both
+projections on N, 2-bit records widened to fp16 in shared memory), through the C ABI.
 
 The kernel takes batches of at least ``FFNRM_PREFILL_TOKENS`` tokens without fallback
 tiles; each test sets that threshold (below the batch where a smaller batch keeps the
-oracle quick). Both operand paths run: the layer's byte codes loaded by TMA, and the
-2-bit records widened in shared memory (``FFNRM_PREFILL_BYTES=0``). Cases: residual bits 1/2/3 (plane and pair records), ragged d_ff (a
+oracle quick). The dots are exact integers computed in fp16 x fp16 -> fp32 (activations
+and low codes exact in fp16), checked bit for bit. Cases: residual bits 1/2/3 (plane and pair records), ragged d_ff (a
 missing second 64-row tile, rows past d_ff inside a tile), ragged token counts, f32
 alphas (not fp16-exact), residual mode (g/u out) and forward mode (h -> down), two token
 tiles with the integer dots checked bit-exact against the oracle's ``group_dots``
@@ -33,13 +33,12 @@ def rel_l2(a, b):
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
 
-def run(cuda, monkeypatch, D, F, T, r, seed, f32_alpha=False, threshold=None, byte_codes=True):
+def run(cuda, monkeypatch, D, F, T, r, seed, f32_alpha=False, threshold=None):
     import torch
     from ffn_residual_mesh_b200 import synth
     from ffn_residual_mesh_b200.engine import LayerSpec, ResidualMesh
     if threshold is not None:
         monkeypatch.setenv("FFNRM_PREFILL_TOKENS", str(threshold))
-    monkeypatch.setenv("FFNRM_PREFILL_BYTES", "1" if byte_codes else "0")
     L = synth.make_layer(3000 + seed, F, D)
     if f32_alpha:
         # scales that fp16 cannot hold exactly: the layer keeps f32 alphas on the device
@@ -82,11 +81,9 @@ CASES = [
 ]
 
 
-@pytest.mark.parametrize("byte_codes", [True, False], ids=["byte_codes", "widened_records"])
 @pytest.mark.parametrize("name,D,F,T,r,f32_alpha,threshold", CASES, ids=[c[0] for c in CASES])
-def test_prefill_parity(name, D, F, T, r, f32_alpha, threshold, byte_codes, cuda, monkeypatch):
-    L, z, out, ref = run(cuda, monkeypatch, D, F, T, r, seed=len(name), f32_alpha=f32_alpha, threshold=threshold,
-                         byte_codes=byte_codes)
+def test_prefill_parity(name, D, F, T, r, f32_alpha, threshold, cuda, monkeypatch):
+    L, z, out, ref = run(cuda, monkeypatch, D, F, T, r, seed=len(name), f32_alpha=f32_alpha, threshold=threshold)
     mask = (1 << r) - 1
     np.testing.assert_array_equal(out["dots"][0], O.group_dots(L.gate_codes & mask, z))
     np.testing.assert_array_equal(out["dots"][1], O.group_dots(L.up_codes & mask, z))
