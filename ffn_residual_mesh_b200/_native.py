@@ -28,6 +28,8 @@ SIGNATURES = {
                                   c_void_p, c_void_p, c_void_p]),
     "ffnrm_ffn_forward_host": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p,
                                        c_void_p, c_void_p]),
+    "ffnrm_ffn_forward_host_partial": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p,
+                                               c_void_p, c_void_p, c_void_p]),
     "ffnrm_host_register": (c_int, [c_void_p, c_size_t]),
     "ffnrm_host_unregister": (c_int, [c_void_p]),
     "ffnrm_cast_f16": (c_int, [c_void_p, c_void_p, c_int64, c_void_p]),

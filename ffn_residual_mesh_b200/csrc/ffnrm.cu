@@ -989,14 +989,16 @@ int ffnrm_ffn_forward(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s
     return enqueue_down(ctx, layer, tokens, y_f32, y_f16, st);
 }
 
-int ffnrm_ffn_forward_host(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s, int tokens,
-                           const float *gate_base, const float *up_base, const uint8_t *fallback_tiles,
-                           uint16_t *y_f16, void *stream) {
+// Host-streamed forward; y goes to host fp16 `y_f16` or, for a shard of a d_ff-split
+// stack, to the device fp32 partial `y32_dev`.
+static int forward_host_impl(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s, int tokens,
+                             const float *gate_base, const float *up_base, const uint8_t *fallback_tiles,
+                             uint16_t *y_f16, float *y32_dev, void *stream) {
     int rc = check_ctx(ctx, layer);
     if (rc) return rc;
     if ((rc = check_tokens(ctx, tokens))) return rc;
     if (tokens == 0) return FFNRM_OK;  // empty batch
-    if (!z || !s || !gate_base || !up_base || !y_f16) return fail(FFNRM_ERR_ARG, "null host pointer");
+    if (!z || !s || !gate_base || !up_base || (!y_f16 && !y32_dev)) return fail(FFNRM_ERR_ARG, "null host pointer");
     if (!ctx->layers[size_t(layer)].down.ptr)
         return fail(FFNRM_ERR_STATE, "layer %d was loaded without a down projection", layer);
     DeviceGuard guard(ctx->device);
@@ -1045,6 +1047,11 @@ int ffnrm_ffn_forward_host(ffnrm_ctx *ctx, int layer, const int8_t *z, const flo
     if ((rc = enqueue_residual(ctx, layer, ctx->z_dev[sl], ctx->s_dev[sl], tokens, nullptr, nullptr, nullptr, tiles_dev,
                                ctx->base_dev[sl][0], ctx->base_dev[sl][1], st)))
         return rc;
+    if (y32_dev) {
+        if ((rc = enqueue_down(ctx, layer, tokens, y32_dev, nullptr, st))) return rc;
+        FFNRM_CUDA(cudaEventRecord(ctx->slot_free[sl], st));
+        return FFNRM_OK;
+    }
     // A page-locked, device-mapped y (cudaHostAlloc, or cudaHostRegister with mapping) is
     // written by the down projection itself over PCIe; otherwise y goes through device
     // staging and one copy back.
@@ -1060,6 +1067,20 @@ int ffnrm_ffn_forward_host(ffnrm_ctx *ctx, int layer, const int8_t *z, const flo
     FFNRM_CUDA(cudaEventRecord(ctx->slot_free[sl], st));
     if (!y_mapped) FFNRM_CUDA(cudaMemcpyAsync(y_f16, ctx->y16_dev, size_t(tokens) * D * 2, cudaMemcpyDeviceToHost, st));
     return FFNRM_OK;
+}
+
+int ffnrm_ffn_forward_host(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s, int tokens,
+                           const float *gate_base, const float *up_base, const uint8_t *fallback_tiles,
+                           uint16_t *y_f16, void *stream) {
+    if (!y_f16) return fail(FFNRM_ERR_ARG, "null host pointer");
+    return forward_host_impl(ctx, layer, z, s, tokens, gate_base, up_base, fallback_tiles, y_f16, nullptr, stream);
+}
+
+int ffnrm_ffn_forward_host_partial(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s, int tokens,
+                                   const float *gate_base, const float *up_base, const uint8_t *fallback_tiles,
+                                   float *y_f32, void *stream) {
+    if (!y_f32) return fail(FFNRM_ERR_ARG, "null device pointer");
+    return forward_host_impl(ctx, layer, z, s, tokens, gate_base, up_base, fallback_tiles, nullptr, y_f32, stream);
 }
 
 int ffnrm_host_register(void *ptr, size_t bytes) {

@@ -238,6 +238,17 @@ class ResidualMesh:
                                                 _addr(up_base), _addr(fallback_tiles), _addr(y16),
                                                 _stream(stream)))
 
+    def forward_host_partial(self, layer, z, s, gate_base, up_base, y32, fallback_tiles=None, stream=None) -> None:
+        """Host-streamed forward of one d_ff shard: host inputs, device fp32 partial out."""
+        T = self._check_act(z, s)
+        self._check_tf("gate_base", gate_base, T)
+        self._check_tf("up_base", up_base, T)
+        if tuple(y32.shape) != (T, self.d_model):
+            raise ValueError(f"y32 must have shape ({T},{self.d_model})")
+        N.check(self.lib.ffnrm_ffn_forward_host_partial(self.handle, layer, _addr(z), _addr(s), T, _addr(gate_base),
+                                                        _addr(up_base), _addr(fallback_tiles), _addr(y32),
+                                                        _stream(stream)))
+
 
 def host_register(array) -> None:
     """Page-lock a host buffer (numpy array) for async copies."""

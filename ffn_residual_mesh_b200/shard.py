@@ -103,30 +103,29 @@ class ShardedFfnStack:
         cast_f16(y32, y16, stream=stream)
 
     def forward_host(self, layer, z, s, gate_base, up_base, y16, staging=None, fallback_tiles=None):
-        """Host (pinned) buffers in and out. One GPU: the C-ABI host-streamed call.
-        Several: H2D of the shard's inputs, forward, allreduce, D2H of y."""
+        """Host (pinned) buffers in and out. One GPU: the C-ABI host-streamed call. Several:
+        the shard's host-streamed call into its device partial (base upload on the copy
+        stream, overlapping the previous layer), the reduction, one D2H of y."""
         if self.world == 1:
             self.mesh.forward_host(layer, z, s, gate_base, up_base, y16, fallback_tiles=fallback_tiles)
             return
-        import torch
-        st = staging
         T = z.shape[0]
-        zd, sd, gd, ud, yd = st["z"][:T], st["s"][:T], st["gb"][:T], st["ub"][:T], st["y16"][:T]
-        zd.copy_(z, non_blocking=True)
-        sd.copy_(s, non_blocking=True)
-        gd.copy_(gate_base, non_blocking=True)
-        ud.copy_(up_base, non_blocking=True)
-        self.forward(layer, zd, sd, gd, ud, yd)
+        st = staging if staging is not None else self.staging(None)
+        y32, yd = self._partial(T, st["y16"].device), st["y16"][:T]
+        self.mesh.forward_host_partial(layer, z, s, gate_base, up_base, y32, fallback_tiles=fallback_tiles)
+        if self.peer is not None:
+            self.peer.allreduce(y32, y16=yd)
+        else:
+            import torch.distributed as dist
+            dist.all_reduce(y32, group=self.group)
+            cast_f16(y32, yd)
         y16.copy_(yd, non_blocking=True)
 
     def staging(self, device):
-        """Device staging buffers for forward_host with world > 1."""
+        """Device staging of y for forward_host with world > 1."""
         import torch
-        T, D, F, G = self.mesh.max_tokens, self.d_model, self.d_ff, self.d_model // 32
-        return {"z": torch.empty(T, D, dtype=torch.int8, device=device),
-                "s": torch.empty(T, G, device=device),
-                "gb": torch.empty(T, F, device=device), "ub": torch.empty(T, F, device=device),
-                "y16": torch.empty(T, D, dtype=torch.float16, device=device)}
+        device = torch.device("cuda", self.mesh.device) if device is None else device
+        return {"y16": torch.empty(self.mesh.max_tokens, self.d_model, dtype=torch.float16, device=device)}
 
     def close(self):
         if self.peer is not None:

@@ -136,6 +136,15 @@ int ffnrm_ffn_forward_host(ffnrm_ctx *ctx, int layer, const int8_t *z, const flo
                            const float *gate_base, const float *up_base, const uint8_t *fallback_tiles,
                            uint16_t *y_f16, void *stream);
 
+/* The same host-streamed call for one shard of a d_ff-split stack: inputs are HOST
+ * pointers as above, and the output is this shard's fp32 partial y_f32 [T,D] in DEVICE
+ * memory, which the caller then sums over the shards (ffnrm_peer_allreduce). The base
+ * upload runs on the copy stream into the alternating slots exactly as above, so it
+ * overlaps the previous layer's kernels. No counterpart in the one-device reference. */
+int ffnrm_ffn_forward_host_partial(ffnrm_ctx *ctx, int layer, const int8_t *z, const float *s, int tokens,
+                                   const float *gate_base, const float *up_base, const uint8_t *fallback_tiles,
+                                   float *y_f32, void *stream);
+
 /* Page-lock an existing host range for async copies (cudaHostRegister) and undo it.
  * Replaces the runners' cudaMallocHost packet staging. */
 int ffnrm_host_register(void *ptr, size_t bytes);

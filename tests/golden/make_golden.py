@@ -12,6 +12,8 @@ the reference's ``scripts/`` directory, never by this repository's oracle:
   ``projection_from_group_dots``  (scripts/benchmark_exact_radix_split_pipeline.py)
 * ``pack_row_codes`` (scripts/export_cuda_residual_artifact_v2.py)
 * ``pack_bitplanes`` (scripts/compile_q4k_host_base_gpu_residual.py)
+* ``load_q4k_codes`` via compile_q4k_host_base_gpu_residual.py main() and
+  export_down_fp16.py main() on a GGUF file written with the ``gguf`` package
 * ``host_gpu_replay`` (scripts/scan_q4k_host_base_gpu_residual.py) for batched
   host-base / residual / merged projections at r = 1, 2, 3
 * the SwiGLU + down formula of scripts/benchmark_cpu_base_gpu_full_ffn.py:369-370.
@@ -82,6 +84,8 @@ def main() -> None:
 
     if args.only is None or "artifacts" in args.only:
         make_artifacts()
+    if args.only is None or "gguf" in args.only:
+        make_gguf()
 
     for name, (F, D, T, r, outliers, seed, tile_rows, flagged) in CASES.items():
         if args.only is not None and name not in args.only:
@@ -89,6 +93,72 @@ def main() -> None:
         make_case(name, F, D, T, r, outliers, seed, tile_rows, flagged, torch, compile_radix_table, direct_group_dots,
                   encode_signed_base4_states, evaluate_radix_table, pack_bitplanes, pack_row_codes, host_gpu_replay,
                   projection_from_group_dots, quantize_groupwise_q8)
+
+
+def make_gguf():
+    """``q4k_layer.gguf``: one synthetic FFN layer (d_model 256, d_ff 256) in a GGUF file
+    written by the ``gguf`` package (the reference's own GGUF dependency): gate and up
+    Q4_K blocks and a Q6_K down, every byte seeded-random except the fp16 block scales
+    (small normals), plus metadata of several value types. From it, the reference's
+    own code writes the expected outputs:
+
+    * ``artifact_q4k_r2/``: scripts/compile_q4k_host_base_gpu_residual.py main() at r = 2
+      (bit planes, alpha, beta and manifest, which records sha256 of each stream);
+    * ``q4k_down.json``: shape and sha256 of the fp16 bytes that scripts/export_down_fp16.py
+      main() writes for the down projection."""
+    import hashlib
+    import json
+    import tempfile
+
+    import compile_q4k_host_base_gpu_residual as comp
+    import export_down_fp16 as exdown
+    from gguf import GGMLQuantizationType as Q
+    from gguf import GGUFWriter
+    rng = np.random.default_rng(909)
+    F, D = 256, 256
+
+    def blocks(rows, nblk, nbytes, f16_at):
+        b = rng.integers(0, 256, size=(rows, nblk, nbytes), dtype=np.uint8)
+        for off in f16_at:
+            v = (rng.standard_normal((rows, nblk)) * 0.01).astype(np.float16)
+            b[:, :, off:off + 2] = v.view(np.uint8).reshape(rows, nblk, 2)
+        return b.reshape(rows, -1)
+
+    path = HERE / "q4k_layer.gguf"
+    w = GGUFWriter(str(path), "llama")
+    w.add_uint32("ffnrm.test.u32", 7)
+    w.add_array("ffnrm.test.array", [1, 2, 3])
+    w.add_string("ffnrm.test.string", "synthetic")
+    w.add_float32("ffnrm.test.f32", 0.5)
+    w.add_tensor("blk.0.ffn_gate.weight", blocks(F, D // 256, 144, [0, 2]), raw_dtype=Q.Q4_K)
+    w.add_tensor("blk.0.ffn_up.weight", blocks(F, D // 256, 144, [0, 2]), raw_dtype=Q.Q4_K)
+    w.add_tensor("blk.0.ffn_down.weight", blocks(D, F // 256, 210, [208]), raw_dtype=Q.Q6_K)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    argv, cwd = sys.argv, os.getcwd()
+    with tempfile.TemporaryDirectory() as tmp:
+        os.chdir(HERE)  # the manifest records the model path: keep it relative
+        try:
+            sys.argv = ["compile", path.name, "--layer", "0", "--residual-bits", "2",
+                        "--out", str(HERE / "artifact_q4k_r2")]
+            comp.main()
+            down = Path(tmp) / "down.f16"
+            sys.argv = ["export", path.name, "--layer", "0", "--out", str(down)]
+            exdown.main()
+            raw = down.read_bytes()
+        finally:
+            sys.argv = argv
+            os.chdir(cwd)
+    man = HERE / "artifact_q4k_r2" / "manifest.json"
+    m = json.loads(man.read_text())
+    m["platform"] = "recorded"  # host-specific text, not part of the contract
+    man.write_text(json.dumps(m, ensure_ascii=False, indent=2), encoding="utf-8")
+    (HERE / "q4k_down.json").write_text(json.dumps(
+        {"shape": [D, F], "dtype": "float16", "bytes": len(raw), "sha256": hashlib.sha256(raw).hexdigest()},
+        indent=2) + "\n")
+    print("gguf ok")
 
 
 def make_artifacts():

@@ -4,7 +4,8 @@ Each rank holds half of the gate/up rows and the matching down columns; the laye
 output is the sum of the ranks' partials, reduced either by the NVLink peer kernel
 (``ffnrm_peer_allreduce``) or by an NCCL allreduce plus a cast. Checked: every rank
 ends with the same output, a CUDA-graph replay reproduces the eager call bit for bit
-(the peer kernel's call counter lives on the device), and the output matches the
+(the peer kernel's call counter lives on the device), so does the host-streamed call
+(``forward_host``: host buffers, device partial, reduction), and the output matches the
 unsharded oracle within the north-star tolerance. Skipped with fewer than two GPUs.
 """
 from __future__ import annotations
@@ -71,7 +72,17 @@ def _rank(rank, world, port, mode, out):
         torch.cuda.synchronize()
         replay = [b["y16"].cpu().numpy().copy() for b in bufs]
         g.close()
-        out.put((rank, eager, replay))
+        # host-streamed call of the shard (pinned buffers in and out, base on the copy
+        # stream into alternating slots): twice, so both slots serve
+        hosted = []
+        for b in bufs:
+            h = {k: b[k].cpu().pin_memory() for k in ("z", "s", "gb", "ub")}
+            y = torch.zeros(b["y16"].shape, dtype=torch.float16).pin_memory()
+            for _ in range(2):
+                stack.forward_host(0, h["z"], h["s"], h["gb"], h["ub"], y)
+            torch.cuda.synchronize()
+            hosted.append(y.numpy().copy())
+        out.put((rank, eager, replay, hosted))
     finally:
         stack.close()
         dist.destroy_process_group()
@@ -92,8 +103,8 @@ def test_two_gpu_sharded_stack(mode):
         p.start()
     got = {}
     for _ in range(2):
-        rank, eager, replay = q.get(timeout=300)
-        got[rank] = (eager, replay)
+        rank, eager, replay, hosted = q.get(timeout=300)
+        got[rank] = (eager, replay, hosted)
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
@@ -108,6 +119,8 @@ def test_two_gpu_sharded_stack(mode):
         np.testing.assert_array_equal(y0, y1)  # every rank holds the same output
         np.testing.assert_array_equal(y0, got[0][1][i])  # graph replay == eager
         np.testing.assert_array_equal(y1, got[1][1][i])
+        np.testing.assert_array_equal(y0, got[0][2][i])  # host-streamed == device-resident
+        np.testing.assert_array_equal(y1, got[1][2][i])
         y = y0.astype(np.float64)
         assert np.abs(y - ref).max() < Y_MAX_ABS
         assert np.linalg.norm(y - ref) / np.linalg.norm(ref) < Y_REL_L2
