@@ -347,7 +347,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     if (lane == 0) atomicExch(p.err, sm100::kErrWaitEmpty);
                     break;
                 } else {
-                    __nanosleep(256);
+                    __nanosleep(128);
                 }
             }
             // No copy may still be in flight when the CTA exits: each lane waits for the final
@@ -362,8 +362,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 bool ok = true;
                 for (int kt = 0; kt < nkt && ok; ++kt) {
                     const int sa = kt % SA, sw = kt % SW;
-                    if (!(ok = sm100::mbar_wait_idle(a_full + sa, (kt / SA) & 1, p.err, sm100::kErrWaitFull, 32) &&
-                               sm100::mbar_wait_idle(w_full + sw, (kt / SW) & 1, p.err, sm100::kErrWaitFull, 32)))
+                    if (!(ok = sm100::mbar_wait(a_full + sa, (kt / SA) & 1, p.err, sm100::kErrWaitFull) &&
+                               sm100::mbar_wait(w_full + sw, (kt / SW) & 1, p.err, sm100::kErrWaitFull)))
                         break;
                     sm100::tc_fence_after();
                     const uint32_t a = sm100::smem_u32(a_ring + sa * (kPfTokens * kPfRowBytes));
@@ -371,7 +371,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     #pragma unroll
                     for (int j = 0; j < 2; ++j) {
                         const int gi = 2 * kt + j, b = gi % kPfBufs;
-                        if (!(ok = sm100::mbar_wait_idle(acc_empty + b, ((gi / kPfBufs) & 1) ^ 1, p.err, sm100::kErrWaitEmpty, 32)))
+                        if (!(ok = sm100::mbar_wait(acc_empty + b, ((gi / kPfBufs) & 1) ^ 1, p.err, sm100::kErrWaitEmpty)))
                             break;
                         sm100::tc_fence_after();
     #pragma unroll
@@ -397,9 +397,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 const int s1 = kt % S1, sw = kt % SW, s4 = kt % S4;
                 if (ok)
                     ok = __all_sync(0xffffffffu,
-                                    sm100::mbar_wait_idle(src_full + s1, (kt / S1) & 1, p.err, sm100::kErrWaitFull, 128) &&
-                                        sm100::mbar_wait_idle(w_empty + sw, ((kt / SW) & 1) ^ 1, p.err, sm100::kErrWaitEmpty, 128) &&
-                                        sm100::mbar_wait_idle(al_empty + s4, ((kt / S4) & 1) ^ 1, p.err, sm100::kErrWaitEmpty, 128));
+                                    sm100::mbar_wait(src_full + s1, (kt / S1) & 1, p.err, sm100::kErrWaitFull) &&
+                                        sm100::mbar_wait(w_empty + sw, ((kt / SW) & 1) ^ 1, p.err, sm100::kErrWaitEmpty) &&
+                                        sm100::mbar_wait(al_empty + s4, ((kt / S4) & 1) ^ 1, p.err, sm100::kErrWaitEmpty));
                 if (ok) {
                     const uint8_t *src = src_ring + s1 * Ly.src_bytes;
                     uint8_t *W = w_ring + sw * (kPfN * kPfRowBytes);

@@ -66,22 +66,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
     return true;
 }
 
-// mbar_wait for roles that wait most of the time (producers, MMA issuers, helpers): between
-// failed tests the thread sleeps `ns` nanoseconds, leaving its scheduler's issue slots to
-// the warps that compute.
-__device__ __forceinline__ bool mbar_wait_idle(uint64_t *bar, uint32_t parity, int *err, int code, uint32_t ns) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const long long start = clock64();
-    while (!mbar_try_wait(bar, parity)) {
-        if (clock64() - start > kWaitCycles) {
-            if (err) atomicExch(err, code);
-            return false;
-        }
-        __nanosleep(ns);
-    }
-    return true;
-}
-
 // Programmatic dependent launch. grid_dependency_wait() blocks until the preceding
 // kernel of the stream has completed and its memory is visible (a no-op when the kernel
 // was not launched as a dependent); trigger_dependents() lets the next kernel of the

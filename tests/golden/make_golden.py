@@ -99,7 +99,7 @@ def make_gguf():
     """``q4k_layer.gguf``: one synthetic FFN layer (d_model 256, d_ff 256) in a GGUF file
     written by the ``gguf`` package (the reference's own GGUF dependency): gate and up
     Q4_K blocks and a Q6_K down, every byte seeded-random except the fp16 block scales
-    (small normals), plus metadata of several value types. From it, the reference's
+    (|normal| sized so that dequantised weights are about 0.02), plus metadata of several value types. From it, the reference's
     own code writes the expected outputs:
 
     * ``artifact_q4k_r2/``: scripts/compile_q4k_host_base_gpu_residual.py main() at r = 2
@@ -117,10 +117,11 @@ def make_gguf():
     rng = np.random.default_rng(909)
     F, D = 256, 256
 
-    def blocks(rows, nblk, nbytes, f16_at):
+    def blocks(rows, nblk, nbytes, f16_at, scale):
+        # block scales of the size real weights have (|w| ~ 0.02 after dequantisation)
         b = rng.integers(0, 256, size=(rows, nblk, nbytes), dtype=np.uint8)
         for off in f16_at:
-            v = (rng.standard_normal((rows, nblk)) * 0.01).astype(np.float16)
+            v = (np.abs(rng.standard_normal((rows, nblk))) * scale).astype(np.float16)
             b[:, :, off:off + 2] = v.view(np.uint8).reshape(rows, nblk, 2)
         return b.reshape(rows, -1)
 
@@ -130,9 +131,9 @@ def make_gguf():
     w.add_array("ffnrm.test.array", [1, 2, 3])
     w.add_string("ffnrm.test.string", "synthetic")
     w.add_float32("ffnrm.test.f32", 0.5)
-    w.add_tensor("blk.0.ffn_gate.weight", blocks(F, D // 256, 144, [0, 2]), raw_dtype=Q.Q4_K)
-    w.add_tensor("blk.0.ffn_up.weight", blocks(F, D // 256, 144, [0, 2]), raw_dtype=Q.Q4_K)
-    w.add_tensor("blk.0.ffn_down.weight", blocks(D, F // 256, 210, [208]), raw_dtype=Q.Q6_K)
+    w.add_tensor("blk.0.ffn_gate.weight", blocks(F, D // 256, 144, [0, 2], 5e-5), raw_dtype=Q.Q4_K)
+    w.add_tensor("blk.0.ffn_up.weight", blocks(F, D // 256, 144, [0, 2], 5e-5), raw_dtype=Q.Q4_K)
+    w.add_tensor("blk.0.ffn_down.weight", blocks(D, F // 256, 210, [208], 1e-5), raw_dtype=Q.Q6_K)
     w.write_header_to_file()
     w.write_kv_data_to_file()
     w.write_tensors_to_file()
