@@ -18,9 +18,10 @@ layer's data is L2 resident when it runs again and no explicit flush is needed.
 
 * ``value``  - tokens/s with inputs (activations, base sums) resident in HBM, one CUDA
   graph replay per step.
-* ``e2e``    - the same through the public host API (``ffnrm_ffn_forward_host``):
-  pinned host activations and base sums copied in on a side stream, y written back
-  to pinned host memory.
+* ``e2e``    - the same end to end: every call's activations come from pinned host
+  memory and its y goes back to pinned host memory, on side streams that overlap the
+  neighbouring layers' kernels; batches whose base is host-streamed go through the public
+  host-streamed call (``ffnrm_ffn_forward_host``), which also copies the base sums in.
 * N > 1 ranks (torchrun): d_ff sharded, row-parallel down, one reduction of the fp32
   partial per layer over NVLink; value = all tokens / max-over-ranks time.
 * ``--impl reference``: the reference's own AVX2 CPU implementation of the path
@@ -62,6 +63,7 @@ def parse():
     ap.add_argument("--eager", action="store_true", help="time eager calls instead of CUDA-graph replays")
     ap.add_argument("--layers", type=int, default=None, help="override the stack depth (profiling cases)")
     ap.add_argument("--tokens", type=str, default=None, help="override the batches, e.g. 2048 or 1,8")
+    ap.add_argument("--d-ff", type=int, default=None, help="override d_ff (small profiling cases)")
     return ap.parse_args()
 
 
@@ -251,6 +253,8 @@ def run_ours(args, cfg, rank, world, local_rank):
                     g, u = sums["gb"] + sums["gr"], sums["ub"] + sums["ur"]
                     check[T] = (g / (1 + torch.exp(-g)) * u) @ L.down.float().t()
                 del sums
+        if l == 0:
+            down0 = L.down  # for the torch.mm comparison of the down projection
         del L
     torch.cuda.synchronize()
     setup_s = time.perf_counter() - t_setup
@@ -266,7 +270,8 @@ def run_ours(args, cfg, rank, world, local_rank):
         if T in check:
             y, ref = b["y16"].float(), check[T]
             self_check[str(T)] = {"rel_l2": float((y - ref).norm() / ref.norm()),
-                                  "max_abs": float((y - ref).abs().max())}
+                                  "max_abs": float((y - ref).abs().max()), "ref_max_abs": float(ref.abs().max()),
+                                  "note": "y is fp16: the error is its rounding (2^-11 relative)"}
     check.clear()
     mesh.check_device_error()
 
@@ -275,23 +280,48 @@ def run_ours(args, cfg, rank, world, local_rank):
         # others stream theirs from pinned host memory every call
         return "hbm" in cfg.base_modes and (T >= 128 or "host" not in cfg.base_modes)
 
+    copy_in, copy_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
     def run_batches(batches, host=False):
         def fn():
+            # End to end with the base resident: each call's activations come in from pinned
+            # memory on copy_in and its y goes back on copy_out, overlapping the kernels of
+            # the neighbouring layers; an input set's device buffers are refilled only after
+            # the kernels that read them, and its y is overwritten only after the copy back.
+            main = torch.cuda.current_stream()
+            copy_in.wait_stream(main)
+            copy_out.wait_stream(main)
+            used, read_back = {}, {}
             for T in batches:
                 for l in range(cfg.layers):
                     b = layer_in(T, l)
                     if host and hbm_base(T):
-                        # end to end with the base resident: activations in, y out, per call
-                        h = b["host"]
-                        b["z"].copy_(h["z"], non_blocking=True)
-                        b["s"].copy_(h["s"], non_blocking=True)
+                        h, key = b["host"], id(b)
+                        with torch.cuda.stream(copy_in):
+                            if key in used:
+                                copy_in.wait_event(used[key])
+                            b["z"].copy_(h["z"], non_blocking=True)
+                            b["s"].copy_(h["s"], non_blocking=True)
+                            landed = torch.cuda.Event()
+                            landed.record(copy_in)
+                        main.wait_event(landed)
+                        if key in read_back:
+                            main.wait_event(read_back[key])
                         stack.forward(l, b["z"], b["s"], b["gb"], b["ub"], b["y16"])
-                        h["y16"].copy_(b["y16"], non_blocking=True)
+                        used[key] = torch.cuda.Event()
+                        used[key].record(main)
+                        with torch.cuda.stream(copy_out):
+                            copy_out.wait_event(used[key])
+                            h["y16"].copy_(b["y16"], non_blocking=True)
+                            read_back[key] = torch.cuda.Event()
+                            read_back[key].record(copy_out)
                     elif host:
                         h = b["host"]
                         stack.forward_host(l, h["z"], h["s"], h["gb"], h["ub"], h["y16"], staging=staging)
                     else:
                         stack.forward(l, b["z"], b["s"], b["gb"], b["ub"], b["y16"])
+            main.wait_stream(copy_in)
+            main.wait_stream(copy_out)
         return fn
 
     def timed(fn, steps, warmup):
@@ -393,6 +423,26 @@ def run_ours(args, cfg, rank, world, local_rank):
         per_batch[str(T)] = e
     mesh.check_device_error()
 
+    # The reference's own GPU down projection, torch.mm(h.half(), down.t())
+    # (scripts/benchmark_gpu_full_ffn_density.py:162), on the same weight and batch sizes, beside
+    # this library's down kernel (which multiplies h as fp16 hi + lo, twice the MMAs, for
+    # fp32-level h): CUDA events around 20 back-to-back calls after a warm-up.
+    down_vs_mm = {}
+    for T in cfg.tokens:
+        h16 = torch.randn(T, down0.shape[1], device=dev).half()
+        for _ in range(3):
+            torch.mm(h16, down0.t())
+        torch.cuda.synchronize()
+        a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(20):
+            torch.mm(h16, down0.t())
+        b_.record()
+        torch.cuda.synchronize()
+        ours = per_batch[str(T)].get("down", {}).get("us_per_launch")
+        down_vs_mm[str(T)] = {"torch_mm_fp16_us": a.elapsed_time(b_) / 20 * 1e3, "ffnrm_down_hi_lo_us": ours}
+        del h16
+
     tokens_step = sum(cfg.tokens)
     value = tokens_step * args.steps / (dev_ms / 1e3)
     e2e_value = tokens_step * e2e_steps / (e2e_ms / 1e3)
@@ -453,7 +503,8 @@ def run_ours(args, cfg, rank, world, local_rank):
                                       else "ShardedFfnStack.forward_host -> ffnrm_ffn_forward_host (base streamed)")
                         for T in cfg.tokens) + (" (CUDA graph replay)" if use_graphs else "")},
             "cuda_graphs": use_graphs, "roofline": roofline, "residual_kernel": residual_kernel,
-            "kernels": kern_tot, "per_batch": per_batch, "self_check": self_check, "cpu_baseline": cpu,
+            "kernels": kern_tot, "per_batch": per_batch, "down_vs_torch_mm": down_vs_mm, "self_check": self_check,
+            "cpu_baseline": cpu,
             "gpu_launches": launches_per_step * args.steps, "clocks": clock_info, "setup_s": round(setup_s, 1),
         }))
     stack.close()
@@ -462,9 +513,9 @@ def run_ours(args, cfg, rank, world, local_rank):
 def main():
     args = parse()
     cfg = synth.CONFIGS[args.workload]
-    if args.layers or args.tokens:
+    if args.layers or args.tokens or args.d_ff:
         import dataclasses
-        cfg = dataclasses.replace(cfg, layers=args.layers or cfg.layers,
+        cfg = dataclasses.replace(cfg, layers=args.layers or cfg.layers, d_ff=args.d_ff or cfg.d_ff,
                                   tokens=tuple(int(t) for t in args.tokens.split(",")) if args.tokens else cfg.tokens)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -45,11 +45,12 @@ constexpr int kUmmaK = 64;  // d_ff columns per stage (one 128-byte swizzle row)
 
 template <int N>
 struct DownUmmaCfg {
-    static constexpr int stages = N <= 16 ? 5 : (N <= 32 ? 4 : (N <= 64 ? 3 : 4));
+    // ring depth within 227 KB: 48 KB stages at N = 128, 64 KB at 192, 80 KB at 256
+    static constexpr int stages = N <= 16 ? 5 : (N <= 32 ? 4 : (N <= 64 ? 3 : (N <= 128 ? 4 : (N <= 192 ? 3 : 2))));
     static constexpr int a_bytes = kUmmaM * kUmmaK * 2;  // 16 KB
     static constexpr int b_bytes = N * kUmmaK * 2;       // per part (hi or lo)
     static constexpr int stage_bytes = a_bytes + 2 * b_bytes;
-    static constexpr int tmem_cols = N < 32 ? 32 : N;
+    static constexpr int tmem_cols = N <= 32 ? 32 : (N <= 64 ? 64 : (N <= 128 ? 128 : 256));  // a power of two
     static constexpr size_t smem = size_t(stages) * stage_bytes + 1024 /*align*/ + 256 /*barriers*/;
     static_assert(size_t(stages) * stage_bytes >= size_t(N) * kUmmaM * 4, "partial tile reuses the stage ring");
 };

@@ -165,7 +165,8 @@ struct ffnrm_ctx {
     // (FFNRM_RESIDUAL_KERNEL=bytes|packed|mma)
     int res_kernel = 1;
     int prefill_tokens = 0;  // batches of at least this many tokens (no fallback tiles) take the prefill residual (0 = off)
-    CUtensorMap h_map[4][2];             // h hi/lo views for token tiles 16, 32, 64, 128
+    CUtensorMap h_map[6][2];             // h hi/lo views for token tiles 16, 32, 64, 128, 192, 256
+    int down_wide = 0;                   // token tile of the down GEMM above 128 tokens (0: 128)
     __half *h_hi = nullptr, *h_lo = nullptr;  // [Tm, F16] h = SiLU(g)*u as fp16 hi + lo
     // host-streamed mode staging, double-buffered per call
     int8_t *z_dev[2] = {nullptr, nullptr};
@@ -669,7 +670,9 @@ int enqueue_down(ffnrm_ctx *ctx, int layer, int T, float *y32, uint16_t *y16, cu
     if (T <= 16) return launch_down_t<16>(ctx, L.down_map, 0, p, st);
     if (T <= 32) return launch_down_t<32>(ctx, L.down_map, 1, p, st);
     if (T <= 64) return launch_down_t<64>(ctx, L.down_map, 2, p, st);
-    return launch_down_t<128>(ctx, L.down_map, 3, p, st);
+    if (T <= 128 || ctx->down_wide == 0) return launch_down_t<128>(ctx, L.down_map, 3, p, st);
+    if (ctx->down_wide == 192) return launch_down_t<192>(ctx, L.down_map, 4, p, st);
+    return launch_down_t<256>(ctx, L.down_map, 5, p, st);
 }
 
 // ---------------------------------------------------------------------------
@@ -780,6 +783,10 @@ int ffnrm_create(ffnrm_ctx **out, int device, const ffnrm_config *cfg) {
         ctx->res_kernel = std::strcmp(e, "packed") == 0 ? 0 : std::strcmp(e, "mma") == 0 ? 2 : 1;
     if (const char *e = std::getenv("FFNRM_GEMV_TOKENS")) ctx->gemv_tokens = std::max(1, std::atoi(e));
     if (const char *e = std::getenv("FFNRM_PREFILL_TOKENS")) ctx->prefill_tokens = std::max(0, std::atoi(e));
+    if (const char *e = std::getenv("FFNRM_DOWN_WIDE")) {
+        const int w = std::atoi(e);
+        ctx->down_wide = w == 192 || w == 256 ? w : 0;
+    }
     cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
     const size_t TF = size_t(c.max_tokens) * c.d_ff, TD = size_t(c.max_tokens) * c.d_model;
     const size_t F16 = (size_t(c.d_ff) + 15) / 16 * 16;
@@ -803,8 +810,8 @@ int ffnrm_create(ffnrm_ctx **out, int device, const ffnrm_config *cfg) {
         ffnrm_destroy(ctx);
         return fail(FFNRM_ERR_NOMEM, "workspace allocation failed (max_tokens=%d, d_ff=%d)", c.max_tokens, c.d_ff);
     }
-    const uint32_t tiles[4] = {16, 32, 64, 128};
-    for (int i = 0; i < 4; ++i)
+    const uint32_t tiles[6] = {16, 32, 64, 128, 192, 256};
+    for (int i = 0; i < (c.max_tokens > 128 ? 6 : 4); ++i)  // the wide tiles serve batches above 128
         if (!make_fp16_map(&ctx->h_map[i][0], ctx->h_hi, F16, size_t(c.max_tokens), F16, tiles[i]) ||
             !make_fp16_map(&ctx->h_map[i][1], ctx->h_lo, F16, size_t(c.max_tokens), F16, tiles[i])) {
             ffnrm_destroy(ctx);

@@ -177,9 +177,11 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     } else if (warp == 1) {
         if (lane == 0) {  // MMA issuer
             constexpr uint32_t idesc = sm100::umma_idesc_u8s8_s32(128, N);
-            for (int it = 0; it < nkt; ++it) {
-                const int s = it % S, b = it & 1;
-                if (!sm100::mbar_wait(in_full + s, (it / S) & 1, p.err, sm100::kErrWaitFull)) break;
+            int s = 0;  // it mod S and the ring phase, advanced without a division
+            uint32_t ph = 0;
+            for (int it = 0; it < nkt; ++it, s = s + 1 == S ? 0 : s + 1, ph ^= uint32_t(s == 0)) {
+                const int b = it & 1;
+                if (!sm100::mbar_wait(in_full + s, ph, p.err, sm100::kErrWaitFull)) break;
                 if (!sm100::mbar_wait(acc_empty + b, ((it >> 1) & 1) ^ 1, p.err, sm100::kErrWaitEmpty)) break;
                 sm100::tc_fence_after();
                 const uint32_t a = sm100::smem_u32(ring + s * Cfg::stage_bytes), bz = a + Cfg::b_off;
@@ -219,8 +221,10 @@ __global__ void __launch_bounds__(kTcThreads, 2)
 #pragma unroll
         for (int k = 0; k < NH / 2; ++k) acc[k] = make_float2(0.f, 0.f);
         bool ok = true;
-        for (int e = 0; e < nkt; ++e) {
-            const int b = e & 1, sa = e % (2 * S);
+        int sa = 0;  // alpha slot of K tile e: e mod 2S, advanced without a division
+#pragma unroll 2
+        for (int e = 0; e < nkt; ++e, sa = sa + 1 == 2 * S ? 0 : sa + 1) {
+            const int b = e & 1;
             ok = __all_sync(0xffffffffu, sm100::mbar_wait(acc_full + b, (e >> 1) & 1, p.err, sm100::kErrWaitFull));
             if (!ok) break;
             if (drains) {
