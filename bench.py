@@ -409,7 +409,8 @@ def run_ours(args, cfg, rank, world, local_rank):
                 continue
             us = 1e3 * ms / n
             kk = {"us_per_launch": us, "launches_per_step": n // kstep, "achieved_gbs": alg_b.get(k, 0) / (us * 1e-6) / 1e9,
-                  "dram_bytes_per_launch": traffic_table.get(f"{k}:{cfg.key}:T{T}")}
+                  "dram_bytes_per_launch": (traffic_table[f"{k}:{cfg.key}:T{T}"] * stack.d_ff / cfg.d_ff
+                                            if f"{k}:{cfg.key}:T{T}" in traffic_table else None)}
             if k in alg_ops:
                 kk["tops"] = alg_ops[k] / (us * 1e-6) / 1e12
             if k == "residual":
