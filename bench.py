@@ -148,6 +148,7 @@ class CpuReference:
             n = min(T, token_cap)
             _, z, s = synth.make_activations(7000 + T, n, cfg.d_model, cfg.outlier_fraction)
             self.samples.append((T, n, z, s))
+        self.layer = L
         self.model.forward(*self.samples[0][2:])  # warm the pool and pages
 
     def step(self) -> tuple[float, float]:
@@ -160,6 +161,40 @@ class CpuReference:
             measured += dt
             scaled += dt * (T / n) * self.cfg.layers
         return measured, scaled
+
+    def fused_base(self, tokens: int = 8):
+        """The reference's AVX2 radix-table base evaluator (`fused_base`,
+        src/radix_cpu_kernels.h:143-217) on a sample of gate rows: the CPU side of the
+        reference's split, i.e. the host base producer this library's GPU residual pairs with.
+        Radix 4 (r = 2) only; block 2 (block-4 tables are 16x larger: a 70B layer's would not fit
+        host memory), on as many rows as a 64 MB table holds, so the evaluator's per-call set-up
+        is a small share. Scaled to both projections, every row and layer."""
+        from oracle import ffnrm_oracle as O
+        from oracle import refcpu
+        cfg, L = self.cfg, self.layer
+        if cfg.residual_bits != 2:
+            return None
+        block = 2
+        rows = min(cfg.d_ff, (64 << 20) // (cfg.d_model // block * 4 ** block))
+        G = cfg.d_model // 32
+        q_hi = (L.gate_codes[:rows] >> 2).reshape(rows, G, 32)
+        table, hs = O.compile_radix_table(q_hi, block)
+        # the evaluator's layouts once, outside the timed calls
+        table, hs = np.ascontiguousarray(table), np.ascontiguousarray(hs, dtype=np.int16)
+        al, be = np.ascontiguousarray(L.gate_alpha[:rows]), np.ascontiguousarray(L.gate_beta[:rows])
+        z, s = self.samples[0][2], self.samples[0][3]
+        refcpu.fused_base(table, hs, al, be, z[0], s[0], block, self.threads)
+        t0 = time.perf_counter()
+        for i in range(tokens):
+            k = i % z.shape[0]
+            refcpu.fused_base(table, hs, al, be, z[k], s[k], block, self.threads)
+        per_token_rows = (time.perf_counter() - t0) / tokens
+        per_token_stack = per_token_rows * (2 * cfg.d_ff / rows) * cfg.layers
+        return {"block": block, "rows_sampled": rows, "tokens_sampled": tokens, "threads": self.threads,
+                "ms_per_token_per_layer": per_token_rows * (2 * cfg.d_ff / rows) * 1e3,
+                "base_tokens_per_s_for_the_stack": 1.0 / per_token_stack,
+                "sample": f"gate rows 0..{rows} of one layer, table block {block}; scaled by 2*d_ff/rows "
+                          f"and {cfg.layers} layers"}
 
     def info(self):
         parts = [f"{n} of {T} tokens" for T, n, _, _ in self.samples]
@@ -486,6 +521,10 @@ def run_ours(args, cfg, rank, world, local_rank):
             cpu = ref.info()
             cpu.update(value=tokens_step / min(r[1] for r in runs), unit=UNIT,
                        measured_ms=min(r[0] for r in runs) * 1e3)
+            try:
+                cpu["fused_base"] = ref.fused_base()
+            except Exception as exc:  # informative only
+                cpu["fused_base"] = {"error": str(exc)[:200]}
             ref.close()
         except Exception as exc:  # the baseline is reported, never required
             cpu = {"value": None, "unit": UNIT, "error": str(exc)[:200]}
