@@ -27,6 +27,7 @@ namespace ffnrm {
 constexpr int kPeerMaxRanks = 8;
 constexpr int kPeerMaxChunks = 128;
 constexpr int kPeerThreads = 256;
+constexpr int kPeerUnroll = 4;  // independent 16-byte loads per thread in flight (two-shot copies)
 constexpr long long kPeerWaitCycles = 2000000000LL;  // about one second
 
 struct PeerParams {
@@ -182,7 +183,16 @@ __global__ void __launch_bounds__(kPeerThreads) peer_two_shot_kernel(const PeerT
         range(d, b, e);
         float4 *dst = reinterpret_cast<float4 *>(p.scatter[d] + slot + int64_t(p.rank) * p.stride);
         const float4 *sd = src + int64_t(d) * p.slice / 4;
-        for (int64_t i = b + threadIdx.x; i < e; i += blockDim.x) dst[i] = __ldcg(sd + i);
+        // four independent loads per thread in flight before their (posted) peer stores
+        for (int64_t i0 = b + threadIdx.x; i0 < e; i0 += kPeerUnroll * blockDim.x) {
+            float4 v[kPeerUnroll];
+#pragma unroll
+            for (int u = 0; u < kPeerUnroll; ++u)
+                if (i0 + u * blockDim.x < e) v[u] = __ldcg(sd + i0 + u * blockDim.x);
+#pragma unroll
+            for (int u = 0; u < kPeerUnroll; ++u)
+                if (i0 + u * blockDim.x < e) dst[i0 + u * blockDim.x] = v[u];
+        }
     }
     __threadfence_system();
     __syncthreads();
@@ -199,17 +209,28 @@ __global__ void __launch_bounds__(kPeerThreads) peer_two_shot_kernel(const PeerT
         const float4 *in = reinterpret_cast<const float4 *>(p.scatter[p.rank] + slot);
         const int64_t stride = p.stride / 4;
         if (s_ok) {
-            for (int64_t i = b + threadIdx.x; i < e; i += blockDim.x) {
-                float4 a = __ldcg(in + i);
+            // two elements per thread per pass, each summed over the ranks in rank order
+            for (int64_t i0 = b + threadIdx.x; i0 < e; i0 += 2 * blockDim.x) {
+                const int64_t i1 = i0 + blockDim.x;
+                const bool two = i1 < e;
+                float4 a = __ldcg(in + i0), a1 = two ? __ldcg(in + i1) : make_float4(0.f, 0.f, 0.f, 0.f);
                 for (int k = 1; k < p.world; ++k) {
-                    const float4 v = __ldcg(in + int64_t(k) * stride + i);
+                    const float4 v = __ldcg(in + int64_t(k) * stride + i0);
+                    const float4 v1 = two ? __ldcg(in + int64_t(k) * stride + i1) : make_float4(0.f, 0.f, 0.f, 0.f);
                     a.x += v.x;
                     a.y += v.y;
                     a.z += v.z;
                     a.w += v.w;
+                    a1.x += v1.x;
+                    a1.y += v1.y;
+                    a1.z += v1.z;
+                    a1.w += v1.w;
                 }
-                for (int k = 0; k < p.world; ++k)
-                    reinterpret_cast<float4 *>(p.gather[k] + slot + int64_t(p.rank) * p.stride)[i] = a;
+                for (int k = 0; k < p.world; ++k) {
+                    float4 *g = reinterpret_cast<float4 *>(p.gather[k] + slot + int64_t(p.rank) * p.stride);
+                    g[i0] = a;
+                    if (two) g[i1] = a1;
+                }
             }
         }
     }
@@ -228,13 +249,21 @@ __global__ void __launch_bounds__(kPeerThreads) peer_two_shot_kernel(const PeerT
             range(d, b, e);
             const float4 *g = reinterpret_cast<const float4 *>(p.gather[p.rank] + slot + int64_t(d) * p.stride);
             const int64_t off = int64_t(d) * p.slice / 4;
-            for (int64_t i = b + threadIdx.x; i < e; i += blockDim.x) {
-                const float4 a = __ldcg(g + i);
-                if (p.y32) reinterpret_cast<float4 *>(p.y32)[off + i] = a;
-                if (p.y16) {
-                    __half2 *o = reinterpret_cast<__half2 *>(p.y16) + 2 * (off + i);
-                    o[0] = __floats2half2_rn(a.x, a.y);
-                    o[1] = __floats2half2_rn(a.z, a.w);
+            for (int64_t i0 = b + threadIdx.x; i0 < e; i0 += kPeerUnroll * blockDim.x) {
+                float4 v[kPeerUnroll];
+#pragma unroll
+                for (int u = 0; u < kPeerUnroll; ++u)
+                    if (i0 + u * blockDim.x < e) v[u] = __ldcg(g + i0 + u * blockDim.x);
+#pragma unroll
+                for (int u = 0; u < kPeerUnroll; ++u) {
+                    const int64_t i = i0 + u * blockDim.x;
+                    if (i >= e) break;
+                    if (p.y32) reinterpret_cast<float4 *>(p.y32)[off + i] = v[u];
+                    if (p.y16) {
+                        __half2 *o = reinterpret_cast<__half2 *>(p.y16) + 2 * (off + i);
+                        o[0] = __floats2half2_rn(v[u].x, v[u].y);
+                        o[1] = __floats2half2_rn(v[u].z, v[u].w);
+                    }
                 }
             }
         }
