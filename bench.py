@@ -345,14 +345,16 @@ def run_ours(args, cfg, rank, world, local_rank):
                         stack.forward(l, b["z"], b["s"], b["gb"], b["ub"], b["y16"])
                         used[key] = torch.cuda.Event()
                         used[key].record(main)
-                        with torch.cuda.stream(copy_out):
-                            copy_out.wait_event(used[key])
-                            h["y16"].copy_(b["y16"], non_blocking=True)
-                            read_back[key] = torch.cuda.Event()
-                            read_back[key].record(copy_out)
+                        if rank == 0:  # every rank holds the same y after the reduction: one copy back
+                            with torch.cuda.stream(copy_out):
+                                copy_out.wait_event(used[key])
+                                h["y16"].copy_(b["y16"], non_blocking=True)
+                                read_back[key] = torch.cuda.Event()
+                                read_back[key].record(copy_out)
                     elif host:
                         h = b["host"]
-                        stack.forward_host(l, h["z"], h["s"], h["gb"], h["ub"], h["y16"], staging=staging)
+                        stack.forward_host(l, h["z"], h["s"], h["gb"], h["ub"], h["y16"], staging=staging,
+                                           y_to_host=rank == 0)
                     else:
                         stack.forward(l, b["z"], b["s"], b["gb"], b["ub"], b["y16"])
             main.wait_stream(copy_in)
@@ -537,7 +539,8 @@ def run_ours(args, cfg, rank, world, local_rank):
             "data": "synthetic (seeded; Q4 codes U{0..15}, fp16-exact scales, N(0,1) activations quantised per group)",
             "config": config_block(cfg, world),
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d * world,
-                    "d2h_bytes_per_step": d2h * world, "ms_per_step": e2e_ms / e2e_steps, "steps": e2e_steps,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / e2e_steps, "steps": e2e_steps,
+                    "copies": "every rank uploads its activations; rank 0 alone copies y back",
                     "path": "; ".join(
                         f"T={T}: " + ("z/s H2D + ShardedFfnStack.forward (HBM-resident base) + y D2H" if hbm_base(T)
                                       else "ShardedFfnStack.forward_host -> ffnrm_ffn_forward_host (base streamed)")

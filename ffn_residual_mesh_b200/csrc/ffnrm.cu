@@ -577,7 +577,11 @@ int launch_residual_rb(ffnrm_ctx *ctx, const LayerDev &L, ffnrm::ResidualParams 
         return p.dots ? launch_residual_prefill_t<true>(ctx, L, p, st) : launch_residual_prefill_t<false>(ctx, L, p, st);
     if (ctx->res_kernel == 1 && p.fallback_tiles == nullptr && L.codes8.ptr &&
         ffnrm::ResTcCfg<32, false>::smem(p.G, 2) <= 227 * 1024) {
-        if (p.T <= 16) return half ? launch_residual_tc_t<16, true>(ctx, L, p, st) : launch_residual_tc_t<16, false>(ctx, L, p, st);
+        // 16-token tiles when 32-token ones would leave SMs idle (a d_ff shard's few row tiles at
+        // decode sizes): twice the CTAs, each A tile read twice, mostly from L2.
+        const int row_tiles = (p.F + ffnrm::kTcTileRows - 1) / ffnrm::kTcTileRows;
+        const bool narrow = p.T <= 16 || (p.T <= 64 && row_tiles * ((p.T + 31) / 32) < ctx->num_sms);
+        if (narrow) return half ? launch_residual_tc_t<16, true>(ctx, L, p, st) : launch_residual_tc_t<16, false>(ctx, L, p, st);
         return half ? launch_residual_tc_t<32, true>(ctx, L, p, st) : launch_residual_tc_t<32, false>(ctx, L, p, st);
     }
     if (p.T <= 16) return launch_residual_umma_t<16>(ctx, L, p, st);

@@ -102,7 +102,7 @@ class ShardedFfnStack:
         dist.all_reduce(y32, group=self.group)
         cast_f16(y32, y16, stream=stream)
 
-    def forward_host(self, layer, z, s, gate_base, up_base, y16, staging=None, fallback_tiles=None):
+    def forward_host(self, layer, z, s, gate_base, up_base, y16, staging=None, fallback_tiles=None, y_to_host=True):
         """Host (pinned) buffers in and out. One GPU: the C-ABI host-streamed call. Several:
         the shard's host-streamed call into its device partial (base upload on the copy
         stream, overlapping the previous layer), the reduction, one D2H of y."""
@@ -119,7 +119,8 @@ class ShardedFfnStack:
             import torch.distributed as dist
             dist.all_reduce(y32, group=self.group)
             cast_f16(y32, yd)
-        y16.copy_(yd, non_blocking=True)
+        if y_to_host:  # every rank holds the same y; a caller may read it back on one rank only
+            y16.copy_(yd, non_blocking=True)
 
     def staging(self, device):
         """Device staging of y for forward_host with world > 1."""
