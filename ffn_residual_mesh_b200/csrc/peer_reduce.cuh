@@ -147,6 +147,14 @@ struct PeerTwoShotParams {
     int world, rank;
 };
 
+__device__ __forceinline__ uint2 pack_half4(const float4 a) {
+    const __half2 lo = __floats2half2_rn(a.x, a.y), hi = __floats2half2_rn(a.z, a.w);
+    uint2 w;
+    w.x = *reinterpret_cast<const uint32_t *>(&lo);
+    w.y = *reinterpret_cast<const uint32_t *>(&hi);
+    return w;
+}
+
 __device__ __forceinline__ bool peer_wait_flag(volatile uint32_t *f, uint32_t ep, int *status) {
     const long long t0 = clock64();
     while (int32_t(*f - ep) < 0) {
@@ -226,10 +234,21 @@ __global__ void __launch_bounds__(kPeerThreads) peer_two_shot_kernel(const PeerT
                     a1.z += v1.z;
                     a1.w += v1.w;
                 }
-                for (int k = 0; k < p.world; ++k) {
-                    float4 *g = reinterpret_cast<float4 *>(p.gather[k] + slot + int64_t(p.rank) * p.stride);
-                    g[i0] = a;
-                    if (two) g[i1] = a1;
+                if (p.y32) {
+                    for (int k = 0; k < p.world; ++k) {
+                        float4 *g = reinterpret_cast<float4 *>(p.gather[k] + slot + int64_t(p.rank) * p.stride);
+                        g[i0] = a;
+                        if (two) g[i1] = a1;
+                    }
+                } else {
+                    // fp16 output only: round the sum here, once, and move half the bytes over
+                    // NVLink (the same bits as rounding after the gather)
+                    const uint2 h0 = pack_half4(a), h1 = pack_half4(a1);
+                    for (int k = 0; k < p.world; ++k) {
+                        uint2 *g = reinterpret_cast<uint2 *>(p.gather[k] + slot + int64_t(p.rank) * p.stride);
+                        g[i0] = h0;
+                        if (two) g[i1] = h1;
+                    }
                 }
             }
         }
@@ -249,6 +268,20 @@ __global__ void __launch_bounds__(kPeerThreads) peer_two_shot_kernel(const PeerT
             range(d, b, e);
             const float4 *g = reinterpret_cast<const float4 *>(p.gather[p.rank] + slot + int64_t(d) * p.stride);
             const int64_t off = int64_t(d) * p.slice / 4;
+            if (!p.y32) {  // fp16 sums, already rounded by their owner
+                const uint2 *gh = reinterpret_cast<const uint2 *>(g);
+                uint2 *yh = reinterpret_cast<uint2 *>(p.y16) + off;
+                for (int64_t i0 = b + threadIdx.x; i0 < e; i0 += kPeerUnroll * blockDim.x) {
+                    uint2 v[kPeerUnroll];
+#pragma unroll
+                    for (int u = 0; u < kPeerUnroll; ++u)
+                        if (i0 + u * blockDim.x < e) v[u] = __ldcg(gh + i0 + u * blockDim.x);
+#pragma unroll
+                    for (int u = 0; u < kPeerUnroll; ++u)
+                        if (i0 + u * blockDim.x < e) yh[i0 + u * blockDim.x] = v[u];
+                }
+                continue;
+            }
             for (int64_t i0 = b + threadIdx.x; i0 < e; i0 += kPeerUnroll * blockDim.x) {
                 float4 v[kPeerUnroll];
 #pragma unroll
