@@ -25,7 +25,7 @@
 namespace ffnrm {
 
 constexpr int kPeerMaxRanks = 8;
-constexpr int kPeerMaxChunks = 128;
+constexpr int kPeerMaxChunks = 256;
 constexpr int kPeerThreads = 256;
 constexpr int kPeerUnroll = 4;  // independent 16-byte loads per thread in flight (two-shot copies)
 constexpr long long kPeerWaitCycles = 2000000000LL;  // about one second
