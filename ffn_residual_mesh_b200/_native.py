@@ -35,6 +35,8 @@ SIGNATURES = {
     "ffnrm_cast_f16": (c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
     "ffnrm_peer_create": (c_int, [POINTER(c_void_p), c_int, c_int, c_int, c_int64, c_void_p]),
     "ffnrm_peer_connect": (c_int, [c_void_p, c_void_p]),
+    "ffnrm_ffn_forward_reduced": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p,
+                                          c_void_p, c_void_p, c_void_p]),
     "ffnrm_peer_allreduce": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p]),
     "ffnrm_peer_check": (c_int, [c_void_p, c_void_p]),
     "ffnrm_peer_destroy": (c_int, [c_void_p]),

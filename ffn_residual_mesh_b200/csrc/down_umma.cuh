@@ -33,11 +33,26 @@ namespace ffnrm {
 
 constexpr int kDownMaxSplits = 8;  // portable cluster size
 
+// Output straight into the layer reduction's reduce-scatter slots (d_ff-sharded stack): the
+// element e = t*D + o of this rank's partial belongs to rank e / slice and is stored, over
+// NVLink, at scatter[owner] + slot(epoch) + rank*stride + (e - owner*slice); when a tile's
+// stores are done, every owner it wrote to counts the tile (system-scope atomic on that
+// rank's counter of the call's parity).
+struct DownScatter {
+    float *scatter[8];      // ranks' scatter slot bases (peer addresses), [2][world][stride]
+    uint32_t *counter[8];   // ranks' tile counters [2] (peer addresses)
+    const uint32_t *epoch;  // this rank's reduction call counter (the call in flight is epoch + 1)
+    int64_t slice, stride;
+    int world, rank;
+};
+
 struct DownUmmaParams {
     float *y32;      // [T, D] or null
     __half *y16;     // [T, D] or null
     int *err;        // error word (bounded waits)
     int D, F16, T, splits, kc;  // kc: d_ff columns per slice, a multiple of 64
+    int fused;                   // nonzero: y goes to the reduction's scatter slots `sc` (splits == 1)
+    DownScatter sc;
 };
 
 constexpr int kUmmaM = 128;
@@ -187,6 +202,46 @@ __global__ void __launch_bounds__(128, 1) down_umma_kernel(const __grid_constant
     sm100::tc_fence_after();
     const int row = warp * 32 + lane;
     const int ntok = min(N, p.T - t0);
+    if (p.fused) {
+        // Fused reduce-scatter: rows of this tile are stored into their owner's slot.
+        const DownScatter &q = p.sc;
+        const uint32_t ep = *reinterpret_cast<const volatile uint32_t *>(q.epoch) + 1u;
+        const int64_t slot = int64_t(ep & 1u) * q.world * q.stride + int64_t(q.rank) * q.stride;
+        if (ok) {
+            int64_t e = int64_t(t0) * p.D + m0 + row;
+            int d = int(e / q.slice);
+            int64_t next = int64_t(d + 1) * q.slice;  // first element of the next owner
+#pragma unroll 1
+            for (int c = 0; c < N; c += 16) {
+                if (c >= ntok) break;
+                uint32_t r[16];
+                sm100::tmem_ld16(tmem + (uint32_t(warp * 32) << 16) + c, r);
+                sm100::tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    if (c + j >= ntok) break;
+                    while (e >= next) {
+                        ++d;
+                        next += q.slice;
+                    }
+                    q.scatter[d][slot + (e - (next - q.slice))] = __uint_as_float(r[j]);
+                    e += p.D;
+                }
+            }
+        }
+        sm100::tc_fence_before();
+        __threadfence_system();
+        __syncthreads();
+        if (warp == 0) sm100::tmem_dealloc(tmem, Cfg::tmem_cols);
+        if (threadIdx.x == 0) {
+            // every owner between the tile's first and last element saw some of its rows (a
+            // slice holds at least two token rows)
+            const int d0 = int((int64_t(t0) * p.D + m0) / q.slice);
+            const int d1 = int((int64_t(t0 + ntok - 1) * p.D + m0 + kUmmaM - 1) / q.slice);
+            for (int d = d0; d <= d1 && d < q.world; ++d) atomicAdd_system(q.counter[d] + (ep & 1u), 1u);
+        }
+        return;
+    }
     if (p.splits == 1) {
         if (ok) {
 #pragma unroll

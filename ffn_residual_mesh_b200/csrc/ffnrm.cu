@@ -644,7 +644,7 @@ int launch_down_cluster(const CUtensorMap &wm, const CUtensorMap &hm, const CUte
     const int occ = Cfg::smem <= 113 * 1024 ? 2 : 1;
     const int mt = p.D / ffnrm::kUmmaM, ntile = (p.T + N - 1) / N;
     const int ksteps = (p.F16 + ffnrm::kUmmaK - 1) / ffnrm::kUmmaK;
-    int splits = std::max(1, std::min({ksteps, ffnrm::kDownMaxSplits, occ * num_sms / (mt * ntile)}));
+    int splits = p.fused ? 1 : std::max(1, std::min({ksteps, ffnrm::kDownMaxSplits, occ * num_sms / (mt * ntile)}));
     const int kc_steps = (ksteps + splits - 1) / splits;
     splits = (ksteps + kc_steps - 1) / kc_steps;
     p.splits = splits;
@@ -662,7 +662,20 @@ int launch_down_t(ffnrm_ctx *ctx, const CUtensorMap &wmap, int map_idx, ffnrm::D
     return rc;
 }
 
-int enqueue_down(ffnrm_ctx *ctx, int layer, int T, float *y32, uint16_t *y16, cudaStream_t st) {
+// Token tile of the down GEMM for a batch of T tokens. 192-token tiles give each MMA 1.5x the
+// work of 128-token ones (measured c4 layer at T = 2048: 1.67 ms vs 1.96 ms) but leave fewer,
+// larger tiles: below about 1024 tokens the 128-token grid is faster (T = 512: 0.54 vs 0.60 ms).
+static int down_token_tile(const ffnrm_ctx *ctx, int T) {
+    if (T <= 16) return 16;
+    if (T <= 32) return 32;
+    if (T <= 64) return 64;
+    const int wide = ctx->down_wide < 0 ? (T >= 1024 ? 192 : 0) : ctx->down_wide;
+    return T <= 128 || wide == 0 ? 128 : wide;
+}
+
+// `sc` non-null: the output tiles go straight into the layer reduction's scatter slots.
+int enqueue_down(ffnrm_ctx *ctx, int layer, int T, float *y32, uint16_t *y16, cudaStream_t st,
+                 const ffnrm::DownScatter *sc = nullptr) {
     LayerDev &L = ctx->layers[size_t(layer)];
     if (!L.down.ptr) return fail(FFNRM_ERR_STATE, "layer %d was loaded without a down projection", layer);
     ffnrm::DownUmmaParams p{};
@@ -672,16 +685,18 @@ int enqueue_down(ffnrm_ctx *ctx, int layer, int T, float *y32, uint16_t *y16, cu
     p.D = ctx->cfg.d_model;
     p.F16 = (ctx->cfg.d_ff + 15) / 16 * 16;
     p.T = T;
-    if (T <= 16) return launch_down_t<16>(ctx, L.down_map, 0, p, st);
-    if (T <= 32) return launch_down_t<32>(ctx, L.down_map, 1, p, st);
-    if (T <= 64) return launch_down_t<64>(ctx, L.down_map, 2, p, st);
-    // 192-token tiles give each MMA 1.5x the work of 128-token ones (measured c4 layer at
-    // T = 2048: 1.67 ms vs 1.96 ms) but leave fewer, larger tiles: below about 1024 tokens the
-    // 128-token grid is faster (T = 512: 0.54 ms vs 0.60 ms).
-    const int wide = ctx->down_wide < 0 ? (T >= 1024 ? 192 : 0) : ctx->down_wide;
-    if (T <= 128 || wide == 0) return launch_down_t<128>(ctx, L.down_map, 3, p, st);
-    if (wide == 192) return launch_down_t<192>(ctx, L.down_map, 4, p, st);
-    return launch_down_t<256>(ctx, L.down_map, 5, p, st);
+    if (sc) {
+        p.fused = 1;
+        p.sc = *sc;
+    }
+    switch (down_token_tile(ctx, T)) {
+        case 16: return launch_down_t<16>(ctx, L.down_map, 0, p, st);
+        case 32: return launch_down_t<32>(ctx, L.down_map, 1, p, st);
+        case 64: return launch_down_t<64>(ctx, L.down_map, 2, p, st);
+        case 128: return launch_down_t<128>(ctx, L.down_map, 3, p, st);
+        case 192: return launch_down_t<192>(ctx, L.down_map, 4, p, st);
+        default: return launch_down_t<256>(ctx, L.down_map, 5, p, st);
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -1134,6 +1149,7 @@ struct ffnrm_peer {
     void *mapped[ffnrm::kPeerMaxRanks] = {};  // peers' regions opened here (own: region)
     uint32_t *counters = nullptr;              // epoch, done
     int *status = nullptr;
+    float *partial = nullptr;                  // [max_elems] f32: the fused call's partial when it does not fuse
     bool connected = false;
 };
 
@@ -1161,8 +1177,9 @@ int ffnrm_peer_create(ffnrm_peer **out, int device, int world, int rank, int64_t
     pr->two_off = pr->recv_bytes + flag_bytes;
     pr->region_bytes = pr->two_off;
     if (max_elems > pr->one_max) {
+        // scatter and gather slots, their flags, and the fused call's tile counters [2]
         pr->stride = ((max_elems + world - 1) / world + 3) / 4 * 4;
-        pr->region_bytes += size_t(4) * world * size_t(pr->stride) * 4 + 2 * flag_bytes;
+        pr->region_bytes += size_t(4) * world * size_t(pr->stride) * 4 + 2 * flag_bytes + 256;
     }
     cudaIpcMemHandle_t h;
     const bool ok = cudaMalloc(&pr->region, pr->region_bytes) == cudaSuccess &&
@@ -1171,6 +1188,7 @@ int ffnrm_peer_create(ffnrm_peer **out, int device, int world, int rank, int64_t
                     cudaMemset(pr->counters, 0, 2 * sizeof(uint32_t)) == cudaSuccess &&
                     cudaMalloc(&pr->status, sizeof(int)) == cudaSuccess &&
                     cudaMemset(pr->status, 0, sizeof(int)) == cudaSuccess &&
+                    cudaMalloc(&pr->partial, size_t(max_elems) * 4) == cudaSuccess &&
                     cudaIpcGetMemHandle(&h, pr->region) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
     if (!ok) {
         const cudaError_t e = cudaGetLastError();
@@ -1202,6 +1220,45 @@ int ffnrm_peer_connect(ffnrm_peer *pr, const void *ipc_handles) {
     return FFNRM_OK;
 }
 
+// The two-shot reduction of `elems` (> one_max) elements. tiles_expected > 0: fused mode —
+// every rank's down projection has already stored its tiles into the scatter slots and counts
+// them on the owner; the kernel waits for that count instead of scattering `partial`.
+static int launch_two_shot(ffnrm_peer *pr, const float *partial, int64_t elems, uint16_t *y16, float *y32,
+                           uint32_t tiles_expected, cudaStream_t stream) {
+    ffnrm::PeerTwoShotParams q{};
+    const size_t slot_bytes = size_t(2) * pr->world * size_t(pr->stride) * 4;
+    const size_t flag_bytes = size_t(pr->world) * ffnrm::kPeerMaxChunks * 4;
+    for (int k = 0; k < pr->world; ++k) {
+        uint8_t *base = static_cast<uint8_t *>(pr->mapped[k]) + pr->two_off;
+        q.scatter[k] = reinterpret_cast<float *>(base);
+        q.gather[k] = reinterpret_cast<float *>(base + slot_bytes);
+        q.sflags[k] = reinterpret_cast<uint32_t *>(base + 2 * slot_bytes);
+        q.gflags[k] = reinterpret_cast<uint32_t *>(base + 2 * slot_bytes + flag_bytes);
+    }
+    if (tiles_expected) {
+        q.tiles = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(pr->region) + pr->two_off + 2 * slot_bytes +
+                                               2 * flag_bytes);
+        q.tiles_expected = tiles_expected;
+    }
+    q.partial = partial;
+    q.y16 = reinterpret_cast<__half *>(y16);
+    q.y32 = y32;
+    q.epoch = pr->counters;
+    q.done = pr->counters + 1;
+    q.status = pr->status;
+    q.elems = elems;
+    q.slice = ((elems + pr->world - 1) / pr->world + 3) / 4 * 4;
+    q.stride = pr->stride;
+    q.world = pr->world;
+    q.rank = pr->rank;
+    const int64_t per = (q.slice + ffnrm::kPeerMaxChunks - 1) / ffnrm::kPeerMaxChunks;
+    q.chunk = int(std::max<int64_t>(2048, (per + 3) / 4 * 4));
+    const int chunks = int((q.slice + q.chunk - 1) / q.chunk);
+    FFNRM_CUDA(launch_dependent(ffnrm::peer_two_shot_kernel, dim3(unsigned(chunks)), dim3(ffnrm::kPeerThreads), 0,
+                                stream, true, 1, q));
+    return FFNRM_OK;
+}
+
 int ffnrm_peer_allreduce(ffnrm_peer *pr, const float *partial, int64_t elems, uint16_t *y16, float *y32,
                          void *stream) {
     if (!pr || !partial || (!y16 && !y32)) return fail(FFNRM_ERR_ARG, "null argument");
@@ -1212,35 +1269,7 @@ int ffnrm_peer_allreduce(ffnrm_peer *pr, const float *partial, int64_t elems, ui
     if (!aligned(partial, 16) || (y32 && !aligned(y32, 16)) || (y16 && !aligned(y16, 8)))
         return fail(FFNRM_ERR_ARG, "partial and y32 must be 16-byte aligned, y16 8-byte aligned");
     DeviceGuard guard(pr->device);
-    if (elems > pr->one_max) {
-        ffnrm::PeerTwoShotParams q{};
-        const size_t slot_bytes = size_t(2) * pr->world * size_t(pr->stride) * 4;
-        const size_t flag_bytes = size_t(pr->world) * ffnrm::kPeerMaxChunks * 4;
-        for (int k = 0; k < pr->world; ++k) {
-            uint8_t *base = static_cast<uint8_t *>(pr->mapped[k]) + pr->two_off;
-            q.scatter[k] = reinterpret_cast<float *>(base);
-            q.gather[k] = reinterpret_cast<float *>(base + slot_bytes);
-            q.sflags[k] = reinterpret_cast<uint32_t *>(base + 2 * slot_bytes);
-            q.gflags[k] = reinterpret_cast<uint32_t *>(base + 2 * slot_bytes + flag_bytes);
-        }
-        q.partial = partial;
-        q.y16 = reinterpret_cast<__half *>(y16);
-        q.y32 = y32;
-        q.epoch = pr->counters;
-        q.done = pr->counters + 1;
-        q.status = pr->status;
-        q.elems = elems;
-        q.slice = ((elems + pr->world - 1) / pr->world + 3) / 4 * 4;
-        q.stride = pr->stride;
-        q.world = pr->world;
-        q.rank = pr->rank;
-        const int64_t per = (q.slice + ffnrm::kPeerMaxChunks - 1) / ffnrm::kPeerMaxChunks;
-        q.chunk = int(std::max<int64_t>(2048, (per + 3) / 4 * 4));
-        const int chunks = int((q.slice + q.chunk - 1) / q.chunk);
-        FFNRM_CUDA(launch_dependent(ffnrm::peer_two_shot_kernel, dim3(unsigned(chunks)), dim3(ffnrm::kPeerThreads), 0,
-                                    static_cast<cudaStream_t>(stream), true, 1, q));
-        return FFNRM_OK;
-    }
+    if (elems > pr->one_max) return launch_two_shot(pr, partial, elems, y16, y32, 0, static_cast<cudaStream_t>(stream));
     ffnrm::PeerParams p{};
     for (int k = 0; k < pr->world; ++k) {
         p.recv[k] = static_cast<float *>(pr->mapped[k]);
@@ -1264,6 +1293,65 @@ int ffnrm_peer_allreduce(ffnrm_peer *pr, const float *partial, int64_t elems, ui
     FFNRM_CUDA(launch_dependent(ffnrm::peer_allreduce_kernel, dim3(unsigned(chunks)), dim3(ffnrm::kPeerThreads), 0,
                                 static_cast<cudaStream_t>(stream), true, 1, p));
     return FFNRM_OK;
+}
+
+int ffnrm_ffn_forward_reduced(ffnrm_ctx *ctx, ffnrm_peer *pr, int layer, const int8_t *z, const float *s, int tokens,
+                              const float *gate_base, const float *up_base, const uint8_t *fallback_tiles,
+                              uint16_t *y_f16, void *stream) {
+    int rc = check_ctx(ctx, layer);
+    if (rc) return rc;
+    if ((rc = check_tokens(ctx, tokens))) return rc;
+    if (!pr || !pr->connected) return fail(FFNRM_ERR_STATE, "peer reduction not connected");
+    if (pr->device != ctx->device) return fail(FFNRM_ERR_ARG, "context and peer reduction on different devices");
+    if (tokens == 0) return FFNRM_OK;  // empty batch
+    if (!z || !s || !gate_base || !up_base || !y_f16) return fail(FFNRM_ERR_ARG, "null device pointer");
+    if (!ctx->layers[size_t(layer)].down.ptr)
+        return fail(FFNRM_ERR_STATE, "layer %d was loaded without a down projection", layer);
+    const int D = ctx->cfg.d_model, W = pr->world;
+    const int64_t elems = int64_t(tokens) * D;
+    if (elems > pr->max_elems)
+        return fail(FFNRM_ERR_ARG, "tokens x d_model = %lld exceeds the reduction's %lld", (long long)elems,
+                    (long long)pr->max_elems);
+    if (!aligned(z, 16) || !aligned(s, 4) || !aligned(gate_base, 4) || !aligned(up_base, 4) || !aligned(y_f16, 8))
+        return fail(FFNRM_ERR_ARG, "z must be 16-byte aligned, y_f16 8-byte, s and base sums 4-byte");
+    DeviceGuard guard(ctx->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if ((rc = enqueue_residual(ctx, layer, z, s, tokens, nullptr, nullptr, nullptr, fallback_tiles, gate_base, up_base,
+                               st)))
+        return rc;
+    const int64_t slice = ((elems + W - 1) / W + 3) / 4 * 4;
+    if (elems <= pr->one_max || slice < 2 * int64_t(D)) {
+        // small messages (and slices under two token rows): the down projection writes a
+        // partial, which the reduction then takes as usual
+        if ((rc = enqueue_down(ctx, layer, tokens, pr->partial, nullptr, st))) return rc;
+        return ffnrm_peer_allreduce(pr, pr->partial, elems, y_f16, nullptr, stream);
+    }
+    // Fused: the down projection stores its output tiles into the owners' scatter slots; the
+    // owner of slice r expects one count per (rank, tile) whose rows reach slice r.
+    ffnrm::DownScatter sc{};
+    const size_t slot_bytes = size_t(2) * W * size_t(pr->stride) * 4;
+    const size_t flag_bytes = size_t(W) * ffnrm::kPeerMaxChunks * 4;
+    for (int k = 0; k < W; ++k) {
+        uint8_t *base = static_cast<uint8_t *>(pr->mapped[k]) + pr->two_off;
+        sc.scatter[k] = reinterpret_cast<float *>(base);
+        sc.counter[k] = reinterpret_cast<uint32_t *>(base + 2 * slot_bytes + 2 * flag_bytes);
+    }
+    sc.epoch = pr->counters;
+    sc.slice = slice;
+    sc.stride = pr->stride;
+    sc.world = W;
+    sc.rank = pr->rank;
+    const int N = down_token_tile(ctx, tokens);
+    uint32_t expected = 0;
+    for (int t0 = 0; t0 < tokens; t0 += N)
+        for (int m0 = 0; m0 < D; m0 += ffnrm::kUmmaM) {
+            const int ntok = std::min(N, tokens - t0);
+            const int64_t d0 = (int64_t(t0) * D + m0) / slice;
+            const int64_t d1 = (int64_t(t0 + ntok - 1) * D + m0 + ffnrm::kUmmaM - 1) / slice;
+            if (d0 <= pr->rank && pr->rank <= d1) expected += uint32_t(W);
+        }
+    if ((rc = enqueue_down(ctx, layer, tokens, nullptr, nullptr, st, &sc))) return rc;
+    return launch_two_shot(pr, nullptr, elems, y_f16, nullptr, expected, st);
 }
 
 int ffnrm_peer_check(ffnrm_peer *pr, void *stream) {

@@ -141,6 +141,8 @@ struct PeerTwoShotParams {
     float *y32;
     uint32_t *epoch, *done;
     int *status;
+    uint32_t *tiles;       // this rank's tile counters [2] (fused mode), or null
+    uint32_t tiles_expected;  // fused mode: down-projection tiles (all ranks) that write this rank's slice
     int64_t elems, slice;  // slice: elements per rank (a multiple of 4); the last rank's may be shorter
     int64_t stride;        // elements between ranks' slots (the largest slice the region holds)
     int chunk;             // elements per CTA within a slice, a multiple of 4
@@ -184,9 +186,10 @@ __global__ void __launch_bounds__(kPeerThreads) peer_two_shot_kernel(const PeerT
         b = min(len, int64_t(c) * p.chunk) / 4;
         e = min(len, int64_t(c + 1) * p.chunk) / 4;
     };
-    // 1. scatter: chunk c of every slice d to rank d
+    // 1. scatter: chunk c of every slice d to rank d (done already, tile by tile, by the down
+    //    projection of every rank in fused mode: wait for all of their tiles instead)
     const float4 *src = reinterpret_cast<const float4 *>(p.partial);
-    for (int d = 0; d < p.world; ++d) {
+    for (int d = 0; d < (p.tiles ? 0 : p.world); ++d) {
         int64_t b, e;
         range(d, b, e);
         float4 *dst = reinterpret_cast<float4 *>(p.scatter[d] + slot + int64_t(p.rank) * p.stride);
@@ -204,11 +207,25 @@ __global__ void __launch_bounds__(kPeerThreads) peer_two_shot_kernel(const PeerT
     }
     __threadfence_system();
     __syncthreads();
-    if (threadIdx.x < p.world)
-        *reinterpret_cast<volatile uint32_t *>(p.sflags[threadIdx.x] + p.rank * kPeerMaxChunks + c) = ep;
-    // 2. reduce chunk c of this rank's slice in rank order, push the sum to every rank
-    if (threadIdx.x < p.world && !peer_wait_flag(p.sflags[p.rank] + threadIdx.x * kPeerMaxChunks + c, ep, p.status))
-        s_ok = 0;
+    if (p.tiles) {
+        if (threadIdx.x == 0) {
+            const volatile uint32_t *cnt = p.tiles + (ep & 1u);
+            const long long t0 = clock64();
+            while (*cnt < p.tiles_expected) {
+                if (clock64() - t0 > kPeerWaitCycles) {
+                    atomicExch(p.status, 1);
+                    s_ok = 0;
+                    break;
+                }
+            }
+        }
+    } else {
+        if (threadIdx.x < p.world)
+            *reinterpret_cast<volatile uint32_t *>(p.sflags[threadIdx.x] + p.rank * kPeerMaxChunks + c) = ep;
+        // 2. reduce chunk c of this rank's slice in rank order, push the sum to every rank
+        if (threadIdx.x < p.world && !peer_wait_flag(p.sflags[p.rank] + threadIdx.x * kPeerMaxChunks + c, ep, p.status))
+            s_ok = 0;
+    }
     __syncthreads();
     __threadfence();
     {
@@ -306,6 +323,8 @@ __global__ void __launch_bounds__(kPeerThreads) peer_two_shot_kernel(const PeerT
         __threadfence();
         if (atomicAdd(p.done, 1u) == gridDim.x - 1) {
             *reinterpret_cast<volatile uint32_t *>(p.done) = 0u;
+            // no tile of this parity arrives before this rank's next call has run
+            if (p.tiles) *reinterpret_cast<volatile uint32_t *>(p.tiles + (ep & 1u)) = 0u;
             *reinterpret_cast<volatile uint32_t *>(p.epoch) = ep;
         }
     }

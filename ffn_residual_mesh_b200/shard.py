@@ -77,6 +77,8 @@ class ShardedFfnStack:
         self.peer = None
         if world > 1 and os.environ.get("FFNRM_PEER_REDUCE", "1") != "0":
             self.peer = PeerReduce(world, rank, device, max_tokens * d_model, group=group)
+        # FFNRM_PEER_FUSED=1: down projection and reduce-scatter in one kernel (ffnrm_ffn_forward_reduced)
+        self.fused = os.environ.get("FFNRM_PEER_FUSED", "0") != "0"
 
     @property
     def d_ff(self) -> int:
@@ -92,6 +94,15 @@ class ShardedFfnStack:
         """Device buffers; gate_base/up_base are this rank's [T, F_shard] slices."""
         if self.world == 1:
             self.mesh.forward(layer, z, s, gate_base, up_base, fallback_tiles=fallback_tiles, y16=y16, stream=stream)
+            return
+        if self.peer is not None and self.fused:
+            # down projection and reduce-scatter in one kernel, then the sum and all-gather
+            T = self.mesh._check_act(z, s)
+            self.mesh._check_tf("gate_base", gate_base, T)
+            self.mesh._check_tf("up_base", up_base, T)
+            N.check(N.lib().ffnrm_ffn_forward_reduced(self.mesh.handle, self.peer._h, layer, _addr(z), _addr(s), T,
+                                                      _addr(gate_base), _addr(up_base), _addr(fallback_tiles),
+                                                      _addr(y16), _stream(stream)))
             return
         import torch.distributed as dist
         y32 = self._partial(z.shape[0], z.device)

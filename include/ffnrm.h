@@ -175,6 +175,16 @@ int ffnrm_peer_allreduce(ffnrm_peer *peer, const float *partial, int64_t elems, 
                          void *stream);
 int ffnrm_peer_check(ffnrm_peer *peer, void *stream);
 int ffnrm_peer_destroy(ffnrm_peer *peer);
+/* Full split FFN of one d_ff shard with the layer-output reduction fused in: device buffers
+ * as ffnrm_ffn_forward, y_f16 [T, D] the summed layer output (the same on every rank). For
+ * messages above the one-shot limit the down projection stores each output tile straight into
+ * its owner rank's reduce-scatter slot over NVLink and counts the tile there, so the reduction
+ * kernel only sums its slice and all-gathers (fp16); smaller messages take the down projection
+ * into a partial plus ffnrm_peer_allreduce. Every rank makes the same calls in the same order.
+ * No reference counterpart (the reference runs on one device). */
+int ffnrm_ffn_forward_reduced(ffnrm_ctx *ctx, ffnrm_peer *peer, int layer, const int8_t *z, const float *s, int tokens,
+                              const float *gate_base, const float *up_base, const uint8_t *fallback_tiles,
+                              uint16_t *y_f16, void *stream);
 
 /* Device bytes held by loaded weights / workspace (for the bench's byte accounting). */
 int ffnrm_layer_bytes(ffnrm_ctx *ctx, int layer, int64_t *residual_bytes, int64_t *down_bytes);

@@ -3,7 +3,8 @@
 Each rank holds half of the gate/up rows and the matching down columns; the layer
 output is the sum of the ranks' partials, reduced either by the NVLink peer kernel
 (``ffnrm_peer_allreduce``) or by an NCCL allreduce plus a cast. Checked: every rank
-ends with the same output, a CUDA-graph replay reproduces the eager call bit for bit
+ends with the same output (also with the reduce-scatter fused into the down projection,
+``ffnrm_ffn_forward_reduced``), a CUDA-graph replay reproduces the eager call bit for bit
 (the peer kernel's call counter lives on the device), so does the host-streamed call
 (``forward_host``: host buffers, device partial, reduction), and the output matches the
 unsharded oracle within the north-star tolerance. Skipped with fewer than two GPUs.
@@ -19,7 +20,7 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 D, F, R = 512, 1000, 2
-TOKENS = (1, 8, 40)
+TOKENS = (1, 3, 8, 40)  # at the two-shot threshold of 1024: 3 x 512 is two-shot with a slice under two rows
 Y_MAX_ABS, Y_REL_L2 = 1e-2, 1e-3
 
 
@@ -29,10 +30,11 @@ def _rank(rank, world, port, mode, out):
     import torch
     import torch.distributed as dist
     # mode: "1" peer kernel (one-shot below 2^20 elements), "2" peer kernel with the two-shot
-    # reduce-scatter + all-gather from 1024 elements, "0" NCCL allreduce + cast
+    # reduce-scatter + all-gather from 1024 elements, "3" the same with the reduce-scatter fused
+    # into the down projection, "0" NCCL allreduce + cast
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), FFNRM_PEER_REDUCE="0" if mode == "0" else "1",
-                      NCCL_NVLS_ENABLE="0")
-    if mode == "2":
+                      NCCL_NVLS_ENABLE="0", FFNRM_PEER_FUSED="1" if mode == "3" else "0")
+    if mode in ("2", "3"):
         os.environ["FFNRM_PEER_TWO_SHOT"] = "1024"
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
@@ -88,7 +90,7 @@ def _rank(rank, world, port, mode, out):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["1", "2", "0"], ids=["peer", "peer_two_shot", "nccl"])
+@pytest.mark.parametrize("mode", ["1", "2", "3", "0"], ids=["peer", "peer_two_shot", "peer_fused", "nccl"])
 def test_two_gpu_sharded_stack(mode):
     import torch
     if torch.cuda.device_count() < 2:
