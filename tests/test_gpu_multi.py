@@ -95,6 +95,8 @@ def test_two_gpu_sharded_stack(mode):
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
+    if mode == "3" and os.environ.get("FFNRM_TEST_FUSED") != "1":
+        pytest.skip("the fused reduce-scatter is opt-in; FFNRM_TEST_FUSED=1 runs its parity case")
     from ffn_residual_mesh_b200 import synth
     from oracle import ffnrm_oracle as O
     ctx = mp.get_context("spawn")
